@@ -1,0 +1,220 @@
+/* qhtp.h -- C ABI of the B200 (sm_100a) quantized MatMul family and GDN chunk inverse.
+ *
+ * Plain pointers and sizes only.  Every buffer is caller-owned device memory unless stated
+ * otherwise; nothing here allocates device memory.  Work is enqueued on the caller's CUDA
+ * stream (`stream` is a cudaStream_t passed as void*; NULL = legacy default stream) and is
+ * asynchronous unless a function says it synchronizes.
+ *
+ * Reference interfaces replaced (paths inside the zzh-www/qcom_htp tree):
+ *   - handwritten C ABI   example/handwritten_hmx_matmul/include/handwritten_hmx_matmul.h:11-52
+ *       HmStatus, HmPreparedRun, hm_<family>_run_prepared, hm_status_string
+ *   - QNN custom ops       HmxU8I8ToU8MatMul  (example/qnn_hmx_matmul_u8i8/src/HmxU8I8ToU8MatMulOp.cpp:481-792)
+ *                          HmxU8I4ToU8MatMul  (example/qnn_hmx_matmul_w4a8/src/HmxU8I4ToU8MatMulOp.cpp:1113-1122)
+ *                          HmxU16I8ToU16MatMul (example/qnn_hmx_matmul_w8a16/src/HmxU16I8ToU16MatMulOp.cpp)
+ *                          HmxU16I4ToU16MatMul (example/qnn_hmx_matmul_w4a16/src/HmxU16I4ToU16MatMulOp.cpp)
+ *                          HmxU16I16ToU16MatMul (example/qnn_hmx_matmul_w16a16/src/HmxU16I16ToU16MatMulOp.cpp:912,1214)
+ *                          HmxW4LpbqExpandToI8 (example/qnn_hmx_matmul_common/HmxW4LpbqExpandToI8Op.cpp:49-157)
+ *   - GDN solve            gdnbm_solve (example/gdn_native/baremetal/inc/gdnbm.idl:10-12),
+ *                          GdnSolve op (example/gdn_native/solve_op/src/GdnSolveOp.cpp:195-281)
+ */
+#ifndef QHTP_H_
+#define QHTP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: same values and meaning as HmStatus (handwritten_hmx_matmul.h:11-16). */
+typedef enum QhtpStatus {
+  QHTP_STATUS_OK = 0,
+  QHTP_STATUS_INVALID_ARGUMENT = 1,
+  QHTP_STATUS_UNSUPPORTED = 2,
+  QHTP_STATUS_RUNTIME_ERROR = 3
+} QhtpStatus;
+
+/* Replaces hm_status_string (handwritten_hmx_matmul.h:52). */
+const char *qhtp_status_string(QhtpStatus status);
+
+/* ------------------------------------------------------------------------------------------
+ * Quantized MatMul:  out[M,N] = requant( act[M,K] (x) weight[N,K] + bias )
+ *
+ * Semantics (QNN affine, offset = -zero_point):  x = (x_q + act_offset) * act_scale,
+ * w = deq(w_q), b = bias_q * act_scale * weight_scale[n],
+ * out_q = clip(round_half_even(y / out_scale - out_offset), 0, 2^out_bits - 1).
+ * Dequant modes:
+ *   QHTP_DEQUANT_F32_WEIGHT  deq(w_q) = float32(w_q * weight_scale[n]) -- the reference oracle's
+ *                            rule (scripts/generate_qnn_matmul_python_cases.py:307,361); outputs
+ *                            are bit-exact to it.
+ *   QHTP_DEQUANT_EXACT       deq(w_q) = w_q * weight_scale[n] exactly (W16A16 semantics,
+ *                            docs/w16a16_is_two_w8a16.md:14-36).
+ * ------------------------------------------------------------------------------------------ */
+typedef enum QhtpFamily {
+  QHTP_FAMILY_U8I8 = 0,   /* u8 act  x int8 weight  -> u8   */
+  QHTP_FAMILY_W4A8 = 1,   /* u8 act  x int4 weight  -> u8   */
+  QHTP_FAMILY_W8A16 = 2,  /* u16 act x int8 weight  -> u16  */
+  QHTP_FAMILY_W4A16 = 3,  /* u16 act x int4 weight  -> u16  */
+  QHTP_FAMILY_W16A16 = 4  /* u16 act x int16 weight -> u16 (two byte-weight passes) */
+} QhtpFamily;
+
+typedef enum QhtpWeightSchema {
+  QHTP_SCHEMA_PER_CHANNEL = 0, /* symmetric per-output-channel scale                         */
+  QHTP_SCHEMA_LPBQ = 1         /* int4 x per-block uint8 factor (1..16) x per-channel scale;  */
+                               /* expanded exactly like HmxW4LpbqExpandToI8Op.cpp:94-97        */
+} QhtpWeightSchema;
+
+typedef enum QhtpDequant {
+  QHTP_DEQUANT_F32_WEIGHT = 0,
+  QHTP_DEQUANT_EXACT = 1
+} QhtpDequant;
+
+/* Weight-side inputs (all device pointers).
+ * weight layout by family:
+ *   U8I8, W8A16 : int8  [N, K] row-major (the reference's weight_q_nk)
+ *   W4A8, W4A16 : int4 K-pair bytes [K/2, N]: byte (k>>1)*N + n, even k in the low nibble,
+ *                 two's-complement nibbles (HmxW4LpbqExpandToI8Op.cpp:5,32-40)
+ *   W16A16      : int16 [N, K] row-major
+ * lpbq_block_scale: uint8 [N, K/lpbq_block] (n*(K/lpbq_block) + kb), LPBQ only, else NULL. */
+typedef struct QhtpMatmulWeights {
+  uint32_t family;      /* QhtpFamily       */
+  uint32_t schema;      /* QhtpWeightSchema */
+  uint32_t dequant;     /* QhtpDequant      */
+  uint32_t k;
+  uint32_t n;
+  uint32_t lpbq_block;  /* 32 or 64 (multiple of 32, divides K); 0 when not LPBQ */
+  const void *weight;
+  const float *weight_scale;         /* [N] float32, finite, > 0, normal */
+  const int32_t *bias_q;             /* [N] int32                        */
+  const uint8_t *lpbq_block_scale;
+  double act_scale;
+  int32_t act_offset;                /* QNN offset = -zero_point (-128 for u8, -32768 for u16) */
+  double out_scale;
+  int32_t out_offset;                /* 0 for u8 outputs, -32768 for u16 outputs */
+} QhtpMatmulWeights;
+
+/* Host-side plan: filled by qhtp_matmul_plan (host only) and bound to a prepared device buffer by
+ * qhtp_matmul_prepare.  Treat as opaque; it is plain data and may be copied. */
+typedef struct QhtpMatmulPlan {
+  uint32_t magic;
+  uint32_t family, schema, dequant, k, n, lpbq_block;
+  uint32_t act_bits, weight_bits, out_bits;
+  uint32_t mode;          /* kernel variant */
+  uint32_t a_planes;      /* 1 (u8 act) or 2 (u16 act as hi/lo byte planes) */
+  uint32_t ch_per_tile;   /* output channels per 128-row tile */
+  uint32_t n_tiles;
+  uint32_t k_pad;         /* K rounded up to 128 */
+  int32_t act_zp, out_zp, out_qmax;
+  double act_scale, out_scale;
+  uint64_t act_mant;      /* act_scale = act_mant * 2^act_exp2, 53-bit mantissa */
+  int32_t act_exp2;
+  uint64_t out_mant;
+  int32_t out_exp2;
+  uint64_t plane_bytes;   /* prepared weight planes */
+  uint64_t record_bytes;  /* per-channel records (32 bytes each) */
+  uint64_t prepared_bytes;
+  void *prepared;         /* device buffer bound by qhtp_matmul_prepare */
+} QhtpMatmulPlan;
+
+/* Validate shapes / family / schema and fill *plan (host only, no device access).
+ * Requirements: K % 32 == 0, 32 <= K <= 32768, N % 32 == 0, N >= 32; LPBQ only for int4 families. */
+QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights *w, QhtpMatmulPlan *plan);
+
+/* Device bytes qhtp_matmul_prepare needs (== plan->prepared_bytes). */
+size_t qhtp_matmul_prepared_bytes(const QhtpMatmulPlan *plan);
+
+/* Build the prepared record in `prepared` (device, >= prepared_bytes, 256-byte aligned):
+ * byte-plane weights in the tiled layout the kernel streams, and one 32-byte record per output
+ * channel (effective bias, requant multiplier, exact-path exponents).  This is the B200 analogue
+ * of the reference's prepare-time const-fold (HmxW4LpbqExpandToI8Op.cpp:107-157,
+ * gen_quant_chain.py:879).  Synchronizes `stream` to validate the scales. */
+QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan *plan, const QhtpMatmulWeights *w, void *prepared,
+                               size_t prepared_bytes, void *stream);
+
+/* Device workspace qhtp_matmul_run needs for M rows (u16 byte planes + error word). */
+size_t qhtp_matmul_workspace_bytes(const QhtpMatmulPlan *plan, uint32_t m);
+
+/* out[M,N] (u8 or u16, row-major) from act[M,K] (u8 or u16, row-major).  act and out must be
+ * 16-byte aligned.  Asynchronous.  Device-side failures (a timed-out pipeline wait) are reported
+ * by qhtp_matmul_check. */
+QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
+                           void *workspace, size_t workspace_bytes, void *stream);
+
+/* Synchronize `stream` and read the device error word of `workspace`; clears it.  Returns
+ * QHTP_STATUS_RUNTIME_ERROR if a kernel recorded an error (code in *device_code if non-NULL). */
+QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan *plan, void *workspace, uint32_t m, int *device_code,
+                             void *stream);
+
+/* Read back the prepared per-channel records (the B200 "sidecar", 32 bytes per channel, padded to
+ * the tile) into host memory: sizes in bytes.  Synchronizes `stream`. */
+QhtpStatus qhtp_matmul_read_records(const QhtpMatmulPlan *plan, void *host_dst, size_t bytes, void *stream);
+
+/* LPBQ expand (HmxW4LpbqExpandToI8 semantics, HmxW4LpbqExpandToI8Op.cpp:26-47,94-97):
+ * int4 K-pair [K/2, N] x uint8 factor [N, K/block] -> int8 [N, K] row-major, saturated. */
+QhtpStatus qhtp_lpbq_expand_i8(const uint8_t *w4_kpair, const uint8_t *block_scale, uint32_t k, uint32_t n,
+                               uint32_t block, int8_t *out_nk, void *stream);
+
+/* ---- prepared-run entry points, one per family (hm_<family>_run_prepared,
+ *      handwritten_hmx_matmul.h:28-50).  chain > 1 re-applies the same op chain times, each
+ *      output feeding the next activation (requires K == N and equal act/out widths); the
+ *      intermediate results live in `scratch` after the workspace. ---- */
+typedef struct QhtpBuffer {
+  void *data;
+  size_t bytes;
+} QhtpBuffer;
+
+typedef struct QhtpConstBuffer {
+  const void *data;
+  size_t bytes;
+} QhtpConstBuffer;
+
+typedef struct QhtpPreparedRun {
+  uint32_t m, k, n, chain;
+  QhtpConstBuffer activation;   /* device [M,K] */
+  const QhtpMatmulPlan *plan;   /* prepared by qhtp_matmul_prepare */
+  QhtpBuffer scratch;           /* device, >= qhtp_prepared_run_scratch_bytes */
+  QhtpBuffer output;            /* device [M,N] */
+  void *stream;
+} QhtpPreparedRun;
+
+size_t qhtp_prepared_run_scratch_bytes(const QhtpMatmulPlan *plan, uint32_t m, uint32_t chain);
+QhtpStatus qhtp_u8i8_run_prepared(const QhtpPreparedRun *run);
+QhtpStatus qhtp_w4a8_run_prepared(const QhtpPreparedRun *run);
+QhtpStatus qhtp_w8a16_run_prepared(const QhtpPreparedRun *run);
+QhtpStatus qhtp_w4a16_run_prepared(const QhtpPreparedRun *run);
+QhtpStatus qhtp_w16a16_run_prepared(const QhtpPreparedRun *run);
+
+/* ------------------------------------------------------------------------------------------
+ * GDN / KDA chunk triangular inverse  T = (I - A)^-1,  A strictly lower triangular [C, C].
+ * n_chunks independent (batch, head, chunk) matrices, row-major, contiguous.
+ * C in {32, 64, 128, 256}.  Inputs above the diagonal are ignored (treated as zero); the output
+ * upper triangle is written as zero.
+ * ------------------------------------------------------------------------------------------ */
+
+/* A bf16 [n_chunks, C, C] -> T float32 [n_chunks, C, C]. */
+QhtpStatus qhtp_gdn_inverse_bf16(const void *A, float *T, int64_t n_chunks, int32_t C, void *stream);
+
+/* u16-code carrier (gdnbm.idl:10-12, gdn_solve_oc_check.py:28-29): value = (code - zp) * scale.
+ * A codes [n_chunks, C, C] -> T codes, T_code = clip(rint(T / sT) + zpT, 0, 65535). */
+QhtpStatus qhtp_gdn_solve_u16(const uint16_t *A, int64_t n_chunks, int32_t C, int32_t zpA, float sA,
+                              int32_t zpT, float sT, uint16_t *T, void *stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Host-only helpers (no GPU needed).
+ * ------------------------------------------------------------------------------------------ */
+
+/* Library version string. */
+const char *qhtp_version(void);
+
+/* The exact requant decision the kernels use, on the host (for tests):
+ * clip(round_half_even(T*mul*act_mant*2^e2 / (out_mant*2^out_exp2) + zp_out), 0, qmax) with the
+ * same float64 fast path + 128-bit exact tie check as the device epilogue. */
+int32_t qhtp_requant_code_host(int64_t T, double c, uint32_t mul, int32_t e2, uint64_t act_mant,
+                               uint64_t out_mant, int32_t out_exp2, int32_t zp_out, int32_t qmax);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QHTP_H_ */

@@ -1,0 +1,64 @@
+"""Build libqhtp.so (the C-ABI library with the sm_100a kernels) in-tree with nvcc.
+
+    python -m qcom_htp_b200.build            # -> qcom_htp_b200/libqhtp.so
+
+The library is compiled only for sm_100a (B200): tcgen05 / TMA / TMEM instructions are used
+directly, so there is no other target.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+LIB = PKG / "libqhtp.so"
+SOURCES = ["qhtp_abi.cu", "qgemm.cu", "gdn.cu"]
+HEADERS = ["ptx.cuh", "requant.cuh", "internal.h"]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler", "-fPIC,-O2",
+    "-shared",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: the qhtp CUDA library cannot be built")
+
+
+def _stale() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES + HEADERS] + [PKG.parent / "include" / "qhtp.h"]
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
+    if not force and not _stale():
+        return LIB
+    cmd = [nvcc(), *NVCC_FLAGS, *(extra or []), "-o", str(LIB)] + [str(CSRC / s) for s in SOURCES]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    if verbose and r.stderr:
+        print(r.stderr)
+    return LIB
+
+
+if __name__ == "__main__":
+    force = "--force" in sys.argv
+    ptxas_v = "--ptxas-v" in sys.argv
+    out = build(force=force or ptxas_v, verbose=True, extra=["-Xptxas", "-v"] if ptxas_v else None)
+    print(out)

@@ -1,0 +1,60 @@
+// Declarations shared between the .cu translation units of libqhtp (not part of the public ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/qhtp.h"
+
+namespace qhtp {
+
+constexpr uint32_t kPlanMagic = 0x51485450u;  // "QHTP"
+
+// Kernel variants of the quantized GEMM.
+enum GemmMode : uint32_t {
+  kModeF32 = 0,    // f32 weight dequant: B tile = [q (128 ch) | e' (128 ch)], s8
+  kModeExact = 1,  // exact dequant, 8-bit weights: B tile = q (256 ch), s8
+  kModeW16 = 2,    // exact dequant, int16 weights: B tile = [hi s8 (128 ch) | lo u8 (128 ch)]
+};
+
+constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
+constexpr int kTileBRows = 256;  // weight-plane rows per tile
+constexpr int kTileK = 128;      // bytes of K per pipeline stage (one 128-byte swizzle row)
+
+struct ChannelRecord {  // 32 bytes, one per output channel (padded to the tile)
+  int64_t beff;         // effective bias, in accumulator units
+  double c;             // fast-path multiplier: z ~= T * c + zp_out
+  int32_t m_q;          // multiplier of the q-plane accumulator inside T
+  uint32_t mul;         // extra factor of T in the exact tie check
+  int32_t e2;           // binary exponent of the exact tie check
+  int32_t pad;
+};
+static_assert(sizeof(ChannelRecord) == 32, "record layout");
+
+struct GemmLaunch {
+  const QhtpMatmulPlan* plan;
+  const void* act;        // user activation [M,K]
+  uint32_t m;
+  void* out;
+  uint8_t* planes;        // workspace: u16 act byte planes [2][M][K] (A16 only)
+  int* err;               // workspace: device error word
+  cudaStream_t stream;
+};
+
+// qgemm.cu
+cudaError_t launch_gemm(const GemmLaunch& g);
+cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
+                           int* bad_scale, cudaStream_t stream);
+cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k, uint32_t n, uint32_t block,
+                               int8_t* out, cudaStream_t stream);
+
+// gdn.cu
+cudaError_t launch_gdn_bf16(const void* A, float* T, int64_t n_chunks, int C, cudaStream_t stream);
+cudaError_t launch_gdn_u16(const uint16_t* A, int64_t n_chunks, int C, int zpA, float sA, int zpT, float sT,
+                           uint16_t* T, cudaStream_t stream);
+
+// tensor maps (qgemm.cu)
+bool make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                     uint32_t box_inner, uint32_t box_rows);
+
+}  // namespace qhtp

@@ -1,0 +1,549 @@
+// Quantized MatMul family on B200: tcgen05 kind::i8 GEMM with TMEM accumulators, TMA-staged
+// 128-byte-swizzled shared-memory tiles, and a fused exact requant epilogue.
+//
+// Mapping of the reference arithmetic (scripts/generate_qnn_matmul_python_cases.py:426-481) onto
+// integer tensor-core products:
+//   * u8 activations feed the MMA as-is (unsigned A operand); the activation zero-point is folded
+//     into the per-channel effective bias (bias_q - zp * sum_k w, gen_quant_chain.py:879).
+//   * u16 activations are split into two u8 byte planes (hi, lo); each plane is its own MMA into
+//     its own s32 TMEM accumulator, recombined exactly in int64 (256*hi + lo) in the epilogue.
+//   * float32 weight dequant (w_deq = f32(q*s)) is reproduced exactly: s = m_s*2^e_s, and
+//     f32(q*s) = (q*m_s + e')*2^e_s with the integer residual e' in [-64,64].  The prepared weight
+//     tile is [q rows | e' rows]: one N=256 MMA yields both sum(x*q) and sum(x*e').
+//   * int16 weights (W16A16) are two byte planes, hi (s8) and lo (u8) (verify_w16a16_two_w8a16.py:21-48),
+//     giving three accumulators (hi*hi, hi*lo+lo*hi, lo*lo) combined with x65536 / x256 / x1.
+// CTA roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
+// warps 2..5 = epilogue (TMEM -> registers -> int64 combine -> exact requant -> global).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+#include "requant.cuh"
+
+namespace qhtp {
+
+// ------------------------------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched once through the runtime; no -lcuda needed)
+// ------------------------------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                     uint32_t box_inner, uint32_t box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------------------------------------
+// GEMM kernel
+// ------------------------------------------------------------------------------------------------
+struct GemmParams {
+  int M, N, kblocks, a_plane_rows, ch_per_tile;
+  const ChannelRecord* rec;
+  void* out;
+  int zp_out, qmax;
+  uint64_t act_mant, out_mant;
+  int out_exp2;
+  int* err;
+};
+
+template <int PA>
+struct GemmCfg {
+  static constexpr int kStageA = kTileM * kTileK;        // 16 KB per activation plane
+  static constexpr int kStageB = kTileBRows * kTileK;    // 32 KB of weight planes
+  static constexpr int kStage = PA * kStageA + kStageB;
+  static constexpr int kStages = (PA == 1) ? 4 : 3;
+  static constexpr int kRecBytes = 256 * sizeof(ChannelRecord);
+  static constexpr int kSmem = kStages * kStage + kRecBytes + 256 + 1024;
+};
+
+template <int PA, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using Cfg = GemmCfg<PA>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kTmemCols = (PA == 2 || MODE == kModeW16) ? 512 : 256;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  ChannelRecord* srec = reinterpret_cast<ChannelRecord*>(smem + S * Cfg::kStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage + Cfg::kRecBytes);
+  uint64_t* empty = full + S;
+  uint64_t* accf = empty + S;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kTileM;
+  const int tile_n = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp >= 2) {  // stage this tile's channel records in shared memory
+    const uint4* src = reinterpret_cast<const uint4*>(p.rec + static_cast<size_t>(tile_n) * p.ch_per_tile);
+    uint4* dst = reinterpret_cast<uint4*>(srec);
+    for (int i = threadIdx.x - 64; i < p.ch_per_tile * 2; i += 128) dst[i] = src[i];
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        const int s = kb % S;
+        const uint32_t ph = (kb / S) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+        uint8_t* st = stages + s * Cfg::kStage;
+#pragma unroll
+        for (int pl = 0; pl < PA; ++pl)
+          tma_load_2d(st + pl * Cfg::kStageA, &tmA, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
+        tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], kb * kTileK, tile_n * kTileBRows);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        const int s = kb % S;
+        const uint32_t ph = (kb / S) & 1;
+        if (!mbar_wait(&full[s], ph, p.err, kErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(stages + s * Cfg::kStage);
+        const uint64_t dA0 = desc_kmajor_sw128(st);
+        const uint64_t dA1 = desc_kmajor_sw128(st + (PA > 1 ? Cfg::kStageA : 0));
+        const uint64_t dB = desc_kmajor_sw128(st + PA * Cfg::kStageA);
+#pragma unroll
+        for (int kk = 0; kk < kTileK / 32; ++kk) {
+          const uint32_t acc = (kb | kk) ? 1u : 0u;
+          const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
+          if constexpr (MODE == kModeW16) {
+            constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);  // u8 act x s8 hi-byte weight
+            constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);  // u8 act x u8 lo-byte weight
+            const uint64_t dBhi = dB + ko;
+            const uint64_t dBlo = dB + ko + (128 * kTileK >> 4);
+            mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
+            mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
+            mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
+            mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
+          } else {
+            constexpr uint32_t id = idesc_i8(128, 256, 0, 1);
+            mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
+            if constexpr (PA == 2) mma_i8(tmem + 256, dA1 + ko, dB + ko, id, acc);
+          }
+        }
+        mma_commit(&empty[s]);  // stage free once these MMAs have read it
+      }
+      if (ok) mma_commit(accf);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int m = m0 + row;
+    const bool ready = mbar_wait(accf, 0, p.err, kErrTimeoutAccum);
+    tc_fence_after();
+    if (ready) {
+      const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+      const int n_base = tile_n * p.ch_per_tile;
+      const bool u16 = p.qmax > 255;
+      for (int c0 = 0; c0 < p.ch_per_tile; c0 += 16) {
+        uint32_t r0[16], r1[16], r2[16], r3[16];
+        if constexpr (MODE == kModeF32) {
+          tmem_ld16(tl + c0, r0);          // sum x_hi * q   (or x * q for u8 act)
+          tmem_ld16(tl + 128 + c0, r1);    // sum x_hi * e'
+          if constexpr (PA == 2) {
+            tmem_ld16(tl + 256 + c0, r2);  // sum x_lo * q
+            tmem_ld16(tl + 384 + c0, r3);  // sum x_lo * e'
+          }
+        } else if constexpr (MODE == kModeExact) {
+          tmem_ld16(tl + c0, r0);
+          if constexpr (PA == 2) tmem_ld16(tl + 256 + c0, r2);
+        } else {
+          tmem_ld16(tl + c0, r0);          // hi x hi
+          tmem_ld16(tl + 128 + c0, r1);    // hi x lo + lo x hi
+          tmem_ld16(tl + 256 + c0, r2);    // lo x lo
+        }
+        tmem_ld_wait();
+        int32_t code[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const ChannelRecord& rc = srec[c0 + j];
+          int64_t T;
+          if constexpr (MODE == kModeF32) {
+            int64_t pq = static_cast<int32_t>(r0[j]);
+            int64_t pe = static_cast<int32_t>(r1[j]);
+            if constexpr (PA == 2) {
+              pq = pq * 256 + static_cast<int32_t>(r2[j]);
+              pe = pe * 256 + static_cast<int32_t>(r3[j]);
+            }
+            T = static_cast<int64_t>(rc.m_q) * pq + pe + rc.beff;
+          } else if constexpr (MODE == kModeExact) {
+            int64_t pq = static_cast<int32_t>(r0[j]);
+            if constexpr (PA == 2) pq = pq * 256 + static_cast<int32_t>(r2[j]);
+            T = pq + rc.beff;
+          } else {
+            T = static_cast<int64_t>(static_cast<int32_t>(r0[j])) * 65536 +
+                static_cast<int64_t>(static_cast<int32_t>(r1[j])) * 256 + static_cast<int32_t>(r2[j]) + rc.beff;
+          }
+          code[j] = requant_code(T, rc.c, rc.mul, rc.e2, p.act_mant, p.out_mant, p.out_exp2, p.zp_out, p.qmax);
+        }
+        const int n = n_base + c0;
+        if (m < p.M && n < p.N) {
+          if (!u16) {
+            uint8_t* o = reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n;
+            if (n + 16 <= p.N) {
+              uint4 v;
+              v.x = (code[0] & 0xFF) | ((code[1] & 0xFF) << 8) | ((code[2] & 0xFF) << 16) | (code[3] << 24);
+              v.y = (code[4] & 0xFF) | ((code[5] & 0xFF) << 8) | ((code[6] & 0xFF) << 16) | (code[7] << 24);
+              v.z = (code[8] & 0xFF) | ((code[9] & 0xFF) << 8) | ((code[10] & 0xFF) << 16) | (code[11] << 24);
+              v.w = (code[12] & 0xFF) | ((code[13] & 0xFF) << 8) | ((code[14] & 0xFF) << 16) | (code[15] << 24);
+              *reinterpret_cast<uint4*>(o) = v;
+            } else {
+              for (int j = 0; j < 16 && n + j < p.N; ++j) o[j] = static_cast<uint8_t>(code[j]);
+            }
+          } else {
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n;
+            if (n + 16 <= p.N) {
+              uint4 v0, v1;
+              v0.x = code[0] | (code[1] << 16);
+              v0.y = code[2] | (code[3] << 16);
+              v0.z = code[4] | (code[5] << 16);
+              v0.w = code[6] | (code[7] << 16);
+              v1.x = code[8] | (code[9] << 16);
+              v1.y = code[10] | (code[11] << 16);
+              v1.z = code[12] | (code[13] << 16);
+              v1.w = code[14] | (code[15] << 16);
+              reinterpret_cast<uint4*>(o)[0] = v0;
+              reinterpret_cast<uint4*>(o)[1] = v1;
+            } else {
+              for (int j = 0; j < 16 && n + j < p.N; ++j) o[j] = static_cast<uint16_t>(code[j]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// u16 activation [M,K] -> byte planes hi [M,K] and lo [M,K] (u8), the A operands of the A16 GEMM.
+__global__ void split_u16_planes(const uint16_t* __restrict__ act, uint8_t* __restrict__ hi,
+                                 uint8_t* __restrict__ lo, size_t n8) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = reinterpret_cast<const uint4*>(act)[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      h0 |= ((w[j] >> 8) & 0xFFu) << (16 * j);
+      h0 |= ((w[j] >> 24) & 0xFFu) << (16 * j + 8);
+      l0 |= (w[j] & 0xFFu) << (16 * j);
+      l0 |= ((w[j] >> 16) & 0xFFu) << (16 * j + 8);
+      h1 |= ((w[j + 2] >> 8) & 0xFFu) << (16 * j);
+      h1 |= ((w[j + 2] >> 24) & 0xFFu) << (16 * j + 8);
+      l1 |= (w[j + 2] & 0xFFu) << (16 * j);
+      l1 |= ((w[j + 2] >> 16) & 0xFFu) << (16 * j + 8);
+    }
+    reinterpret_cast<uint2*>(hi)[i] = make_uint2(h0, h1);
+    reinterpret_cast<uint2*>(lo)[i] = make_uint2(l0, l1);
+  }
+}
+
+template <int PA, int MODE>
+static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, const CUtensorMap& tb,
+                                  const GemmParams& prm) {
+  using Cfg = GemmCfg<PA>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<PA, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmem);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  dim3 grid((g.m + kTileM - 1) / kTileM, g.plan->n_tiles);
+  qgemm_kernel<PA, MODE><<<grid, 192, Cfg::kSmem, g.stream>>>(ta, tb, prm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const GemmLaunch& g) {
+  const QhtpMatmulPlan* pl = g.plan;
+  const uint32_t K = pl->k;
+  CUtensorMap ta, tb;
+  const uint8_t* a_base;
+  uint64_t a_rows;
+  if (pl->a_planes == 2) {
+    const size_t total = static_cast<size_t>(g.m) * K;
+    const size_t n8 = total / 8;
+    int blocks = static_cast<int>((n8 + 255) / 256);
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks < 1) blocks = 1;
+    split_u16_planes<<<blocks, 256, 0, g.stream>>>(static_cast<const uint16_t*>(g.act), g.planes,
+                                                   g.planes + total, n8);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    a_base = g.planes;
+    a_rows = 2ull * g.m;
+  } else {
+    a_base = static_cast<const uint8_t*>(g.act);
+    a_rows = g.m;
+  }
+  if (!make_tmap_2d_u8(&ta, a_base, K, a_rows, K, kTileK, kTileM)) return cudaErrorInvalidValue;
+  const uint8_t* planes = static_cast<const uint8_t*>(pl->prepared);
+  if (!make_tmap_2d_u8(&tb, planes, pl->k_pad, static_cast<uint64_t>(pl->n_tiles) * kTileBRows, pl->k_pad, kTileK,
+                       kTileBRows))
+    return cudaErrorInvalidValue;
+  GemmParams prm;
+  prm.M = static_cast<int>(g.m);
+  prm.N = static_cast<int>(pl->n);
+  prm.kblocks = static_cast<int>(pl->k_pad / kTileK);
+  prm.a_plane_rows = static_cast<int>(g.m);
+  prm.ch_per_tile = static_cast<int>(pl->ch_per_tile);
+  prm.rec = reinterpret_cast<const ChannelRecord*>(planes + pl->plane_bytes);
+  prm.out = g.out;
+  prm.zp_out = pl->out_zp;
+  prm.qmax = pl->out_qmax;
+  prm.act_mant = pl->act_mant;
+  prm.out_mant = pl->out_mant;
+  prm.out_exp2 = pl->out_exp2;
+  prm.err = g.err;
+  switch (pl->mode * 2 + (pl->a_planes - 1)) {
+    case kModeF32 * 2 + 0: return launch_variant<1, kModeF32>(g, ta, tb, prm);
+    case kModeF32 * 2 + 1: return launch_variant<2, kModeF32>(g, ta, tb, prm);
+    case kModeExact * 2 + 0: return launch_variant<1, kModeExact>(g, ta, tb, prm);
+    case kModeExact * 2 + 1: return launch_variant<2, kModeExact>(g, ta, tb, prm);
+    case kModeW16 * 2 + 1: return launch_variant<2, kModeW16>(g, ta, tb, prm);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Prepare: weight byte planes + per-channel records
+// ------------------------------------------------------------------------------------------------
+struct PrepParams {
+  uint32_t family, schema, mode, K, N, k_pad, ch_per_tile, lpbq_block;
+  const void* weight;
+  const uint8_t* lpbq;
+  int8_t* planes;
+  long long* sums;  // [Npad][2]
+};
+
+__device__ __forceinline__ int load_weight(const PrepParams& p, uint32_t n, uint32_t k) {
+  if (p.family == QHTP_FAMILY_U8I8 || p.family == QHTP_FAMILY_W8A16) {
+    return static_cast<const int8_t*>(p.weight)[static_cast<size_t>(n) * p.K + k];
+  }
+  if (p.family == QHTP_FAMILY_W16A16) {
+    return static_cast<const int16_t*>(p.weight)[static_cast<size_t>(n) * p.K + k];
+  }
+  const uint8_t b = static_cast<const uint8_t*>(p.weight)[static_cast<size_t>(k >> 1) * p.N + n];
+  int q = (k & 1) ? (b >> 4) : (b & 0xF);
+  q = q >= 8 ? q - 16 : q;  // two's-complement nibble
+  if (p.schema == QHTP_SCHEMA_LPBQ) {
+    const int f = p.lpbq[static_cast<size_t>(n) * (p.K / p.lpbq_block) + k / p.lpbq_block];
+    q *= f;
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);  // HmxW4LpbqExpandToI8Op.cpp:42-47
+  }
+  return q;
+}
+
+// One thread per (channel, 16-wide K chunk).
+__global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ scale) {
+  const uint32_t chunks = p.K / 16;
+  const size_t total = static_cast<size_t>(p.N) * chunks;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint32_t n = static_cast<uint32_t>(idx / chunks);
+    const uint32_t k0 = static_cast<uint32_t>(idx % chunks) * 16;
+    const uint32_t tile = n / p.ch_per_tile;
+    const size_t row = static_cast<size_t>(tile) * kTileBRows + (n % p.ch_per_tile);
+    int8_t* r0 = p.planes + row * p.k_pad + k0;
+    long long sq = 0, se = 0;
+    if (p.mode == kModeF32) {
+      const uint32_t bits = __float_as_uint(scale[n]);
+      const int32_t ms = static_cast<int32_t>((bits & 0x7FFFFFu) | 0x800000u);
+      int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int q = load_weight(p, n, k0 + j);
+        const int32_t prod = q * ms;                                    // |prod| < 2^31
+        const int32_t rnd = __float2int_rz(__int2float_rn(prod));     // round to 24 significant bits
+        const int e = rnd - prod;                                       // |e| <= 64
+        r0[j] = static_cast<int8_t>(q);
+        r1[j] = static_cast<int8_t>(e);
+        sq += q;
+        se += e;
+      }
+    } else if (p.mode == kModeExact) {
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int q = load_weight(p, n, k0 + j);
+        r0[j] = static_cast<int8_t>(q);
+        sq += q;
+      }
+    } else {
+      int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int q = load_weight(p, n, k0 + j);
+        r0[j] = static_cast<int8_t>(q >> 8);                  // arithmetic high byte, s8
+        r1[j] = static_cast<int8_t>(static_cast<uint8_t>(q & 0xFF));  // low byte, u8 carrier
+        sq += q;
+      }
+    }
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.sums[2 * n]), static_cast<unsigned long long>(sq));
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.sums[2 * n + 1]), static_cast<unsigned long long>(se));
+  }
+}
+
+__global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* __restrict__ scale,
+                                       const int32_t* __restrict__ bias, const long long* __restrict__ sums,
+                                       double act_scale, double out_scale, int32_t act_zp, int32_t act_exp2,
+                                       ChannelRecord* __restrict__ rec, int* bad_scale) {
+  const uint32_t n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const float s = scale[n];
+  const uint32_t bits = __float_as_uint(s);
+  const uint32_t ex = (bits >> 23) & 0xFFu;
+  ChannelRecord r;
+  r.pad = 0;
+  if ((bits >> 31) != 0 || ex == 0 || ex == 0xFF) {  // negative, zero/subnormal, inf/nan
+    atomicCAS(bad_scale, 0, 1);
+    r.beff = 0;
+    r.c = 0.0;
+    r.m_q = 0;
+    r.mul = 0;
+    r.e2 = 0;
+    rec[n] = r;
+    return;
+  }
+  const int64_t ms = static_cast<int64_t>((bits & 0x7FFFFFu) | 0x800000u);
+  const int es = static_cast<int>(ex) - 150;
+  const int64_t sq = sums[2 * n], se = sums[2 * n + 1];
+  const int64_t b = bias[n];
+  if (mode == kModeF32) {
+    r.beff = ms * (b - static_cast<int64_t>(act_zp) * sq) - static_cast<int64_t>(act_zp) * se;
+    r.c = ldexp(act_scale, es) / out_scale;
+    r.m_q = static_cast<int32_t>(ms);
+    r.mul = 1u;
+  } else {
+    r.beff = b - static_cast<int64_t>(act_zp) * sq;
+    r.c = __dmul_rn(act_scale, static_cast<double>(s)) / out_scale;
+    r.m_q = 1;
+    r.mul = static_cast<uint32_t>(ms);
+  }
+  r.e2 = es + act_exp2;
+  rec[n] = r;
+}
+
+cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared, int* bad_scale,
+                           cudaStream_t stream) {
+  uint8_t* base = static_cast<uint8_t*>(prepared);
+  const size_t npad = static_cast<size_t>(plan->n_tiles) * plan->ch_per_tile;
+  long long* sums = reinterpret_cast<long long*>(base + plan->plane_bytes + plan->record_bytes);
+  cudaError_t e = cudaMemsetAsync(base, 0, plan->prepared_bytes, stream);
+  if (e != cudaSuccess) return e;
+  PrepParams p;
+  p.family = plan->family;
+  p.schema = plan->schema;
+  p.mode = plan->mode;
+  p.K = plan->k;
+  p.N = plan->n;
+  p.k_pad = plan->k_pad;
+  p.ch_per_tile = plan->ch_per_tile;
+  p.lpbq_block = plan->lpbq_block;
+  p.weight = w->weight;
+  p.lpbq = w->lpbq_block_scale;
+  p.planes = reinterpret_cast<int8_t*>(base);
+  p.sums = sums;
+  const size_t total = static_cast<size_t>(plan->n) * (plan->k / 16);
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  prepare_planes_kernel<<<blocks, 256, 0, stream>>>(p, w->weight_scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ChannelRecord* rec = reinterpret_cast<ChannelRecord*>(base + plan->plane_bytes);
+  prepare_records_kernel<<<static_cast<unsigned>((plan->n + 127) / 128), 128, 0, stream>>>(
+      plan->mode, plan->n, w->weight_scale, w->bias_q, sums, plan->act_scale, plan->out_scale, plan->act_zp,
+      plan->act_exp2, rec, bad_scale);
+  (void)npad;
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------
+// Stand-alone LPBQ expand (HmxW4LpbqExpandToI8 semantics), row-major [N,K] int8 output.
+// ------------------------------------------------------------------------------------------------
+__global__ void lpbq_expand_kernel(const uint8_t* __restrict__ w4, const uint8_t* __restrict__ bs, uint32_t K,
+                                   uint32_t N, uint32_t block, int8_t* __restrict__ out) {
+  const size_t total = static_cast<size_t>(N) * K;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint32_t n = static_cast<uint32_t>(i / K), k = static_cast<uint32_t>(i % K);
+    const uint8_t b = w4[static_cast<size_t>(k >> 1) * N + n];
+    int q = (k & 1) ? (b >> 4) : (b & 0xF);
+    q = q >= 8 ? q - 16 : q;
+    q *= bs[static_cast<size_t>(n) * (K / block) + k / block];
+    out[i] = static_cast<int8_t>(q < -128 ? -128 : (q > 127 ? 127 : q));
+  }
+}
+
+cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k, uint32_t n, uint32_t block,
+                               int8_t* out, cudaStream_t stream) {
+  const size_t total = static_cast<size_t>(n) * k;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  lpbq_expand_kernel<<<blocks, 256, 0, stream>>>(w4, bs, k, n, block, out);
+  return cudaGetLastError();
+}
+
+}  // namespace qhtp

@@ -1,0 +1,217 @@
+"""Quantized MatMul family: host side of the B200 replacement for the reference's custom ops.
+
+Reference ops and their counterparts here (all with QNN affine semantics, offset = -zero_point):
+
+  HmxU8I8ToU8MatMul   (example/qnn_hmx_matmul_u8i8/src/HmxU8I8ToU8MatMulOp.cpp:481-792)   family "u8i8"
+  HmxU8I4ToU8MatMul   (example/qnn_hmx_matmul_w4a8/src/HmxU8I4ToU8MatMulOp.cpp:1113-1122) family "w4a8"
+  HmxU16I8ToU16MatMul (example/qnn_hmx_matmul_w8a16/src/HmxU16I8ToU16MatMulOp.cpp)        family "w8a16"
+  HmxU16I4ToU16MatMul (example/qnn_hmx_matmul_w4a16/src/HmxU16I4ToU16MatMulOp.cpp)        family "w4a16"
+  HmxU16I16ToU16MatMul(example/qnn_hmx_matmul_w16a16/src/HmxU16I16ToU16MatMulOp.cpp:1214) family "w16a16"
+  HmxW4LpbqExpandToI8 (example/qnn_hmx_matmul_common/HmxW4LpbqExpandToI8Op.cpp:49-157)    lpbq_expand_i8
+
+Like the reference's QHPI precompute + hot callback split (HmxU8I8ToU8MatMulOp.cpp:218-286 and
+:289), a ``QuantMatMul`` prepares once (weight byte planes, effective bias, requant constants) and
+then each call runs one GEMM kernel.  Unlike the QHPI kernels, which return success on bad inputs,
+every error raises ``QhtpError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+FAMILY_BITS = {"u8i8": (8, 8, 8), "w4a8": (8, 4, 8), "w8a16": (16, 8, 16), "w4a16": (16, 4, 16),
+               "w16a16": (16, 16, 16)}
+
+RECORD_DTYPE = np.dtype([("beff", "<i8"), ("c", "<f8"), ("m_q", "<i4"), ("mul", "<u4"), ("e2", "<i4"),
+                         ("pad", "<i4")])
+
+
+def _stream_handle(stream) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else int(t.data_ptr())
+
+
+def _dt(bits: int) -> torch.dtype:
+    return torch.uint16 if bits == 16 else torch.uint8
+
+
+class QuantMatMul:
+    """A prepared quantized MatMul: out[M,N] = requant(act[M,K] x weight[N,K]^T + bias).
+
+    Parameters (tensors on the CUDA device the op runs on)
+    ----------
+    family        "u8i8" | "w4a8" | "w8a16" | "w4a16" | "w16a16"
+    weight        int8 [N,K] (8-bit), uint8 K-pair [K/2,N] (int4), int16 [N,K] (W16A16)
+    weight_scale  float32 [N] per-output-channel scale (LPBQ: the per-channel base scale)
+    bias_q        int32 [N], quantized at act_scale * weight_scale
+    act_scale/out_scale, act_offset/out_offset  QNN affine parameters (offset = -zero_point);
+                  offsets default to the family's fixed zero points (A8: 128, A16/out16: 32768, out8: 0)
+    schema        "per_channel" | "lpbq"; LPBQ needs lpbq_block_scale uint8 [N, K/lpbq_block]
+    dequant       "f32" (float32 weight dequant, the reference oracle's rule; default for 4/8-bit)
+                  or "exact" (w*s exactly; the only mode for W16A16)
+    """
+
+    def __init__(self, family: str, weight: torch.Tensor, weight_scale: torch.Tensor, bias_q: torch.Tensor, *,
+                 act_scale: float, out_scale: float, act_offset: int | None = None, out_offset: int | None = None,
+                 schema: str = "per_channel", lpbq_block_scale: torch.Tensor | None = None, lpbq_block: int = 0,
+                 dequant: str | None = None, stream=None):
+        if family not in FAMILY_BITS:
+            raise ValueError(f"unknown family {family!r}")
+        a_bits, w_bits, o_bits = FAMILY_BITS[family]
+        if dequant is None:
+            dequant = "exact" if w_bits == 16 else "f32"
+        self.family, self.schema, self.dequant = family, schema, dequant
+        self.act_bits, self.weight_bits, self.out_bits = a_bits, w_bits, o_bits
+        if act_offset is None:
+            act_offset = -(1 << (a_bits - 1))
+        if out_offset is None:
+            out_offset = -32768 if o_bits == 16 else 0
+        if w_bits == 4:
+            k2, n = weight.shape
+            k = 2 * k2
+            want = torch.uint8
+        else:
+            n, k = weight.shape
+            want = torch.int16 if w_bits == 16 else torch.int8
+        if weight.dtype != want:
+            raise TypeError(f"{family}: weight must be {want}, got {weight.dtype}")
+        for name, t in (("weight", weight), ("weight_scale", weight_scale), ("bias_q", bias_q)):
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous CUDA tensor")
+        if weight_scale.dtype != torch.float32 or bias_q.dtype != torch.int32:
+            raise TypeError("weight_scale must be float32 and bias_q int32")
+        if weight_scale.numel() != n or bias_q.numel() != n:
+            raise ValueError("weight_scale / bias_q must have N elements")
+        if schema == "lpbq":
+            if lpbq_block_scale is None or lpbq_block_scale.dtype != torch.uint8:
+                raise ValueError("LPBQ needs lpbq_block_scale uint8 [N, K/block]")
+            if lpbq_block <= 0 or k % lpbq_block or lpbq_block_scale.numel() != n * (k // lpbq_block):
+                raise ValueError("bad LPBQ block / block-scale shape")
+            lpbq_block_scale = lpbq_block_scale.contiguous()
+        self.k, self.n = k, n
+        self.device = weight.device
+        self._keep = [weight, weight_scale, bias_q, lpbq_block_scale]
+        self._w = L.QhtpMatmulWeights(
+            family=L.FAMILY[family], schema=L.SCHEMA[schema], dequant=L.DEQUANT[dequant], k=k, n=n,
+            lpbq_block=lpbq_block if schema == "lpbq" else 0,
+            weight=_ptr(weight), weight_scale=_ptr(weight_scale), bias_q=_ptr(bias_q),
+            lpbq_block_scale=_ptr(lpbq_block_scale),
+            act_scale=float(act_scale), act_offset=int(act_offset), out_scale=float(out_scale),
+            out_offset=int(out_offset))
+        self.plan = L.QhtpMatmulPlan()
+        L.check("qhtp_matmul_plan", L.lib.qhtp_matmul_plan(C.byref(self._w), C.byref(self.plan)))
+        with torch.cuda.device(self.device):
+            self.prepared = torch.empty(int(self.plan.prepared_bytes), dtype=torch.uint8, device=self.device)
+            L.check("qhtp_matmul_prepare", L.lib.qhtp_matmul_prepare(
+                C.byref(self.plan), C.byref(self._w), _ptr(self.prepared), self.prepared.numel(),
+                _stream_handle(stream)))
+        self._ws: dict[int, torch.Tensor] = {}
+
+    # ------------------------------------------------------------------ run
+    def workspace(self, m: int) -> torch.Tensor:
+        ws = self._ws.get(m)
+        if ws is None:
+            nbytes = int(L.lib.qhtp_matmul_workspace_bytes(C.byref(self.plan), m))
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws[m] = ws
+        return ws
+
+    def __call__(self, act: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        if act.dim() != 2 or act.shape[1] != self.k:
+            raise ValueError(f"act must be [M, {self.k}]")
+        if act.dtype != _dt(self.act_bits) or not act.is_cuda or not act.is_contiguous():
+            raise TypeError(f"act must be a contiguous CUDA {_dt(self.act_bits)} tensor")
+        m = act.shape[0]
+        if out is None:
+            out = torch.empty((m, self.n), dtype=_dt(self.out_bits), device=act.device)
+        elif out.shape != (m, self.n) or out.dtype != _dt(self.out_bits) or not out.is_contiguous():
+            raise ValueError("bad output tensor")
+        ws = self.workspace(m)
+        L.check("qhtp_matmul_run", L.lib.qhtp_matmul_run(
+            C.byref(self.plan), _ptr(act), m, _ptr(out), _ptr(ws), ws.numel(), _stream_handle(stream)))
+        return out
+
+    def check_device(self, m: int, stream=None) -> None:
+        """Synchronize and raise if a kernel recorded a device-side error for workspace(m)."""
+        code = C.c_int(0)
+        st = L.lib.qhtp_matmul_check(C.byref(self.plan), _ptr(self.workspace(m)), m, C.byref(code),
+                                     _stream_handle(stream))
+        if st != L.OK:
+            raise L.QhtpError(f"qhtp_matmul_check (device code {code.value})", st)
+
+    def records(self, stream=None) -> np.ndarray:
+        """The prepared per-channel records (the B200 "sidecar"), padded to the channel tile."""
+        npad = int(self.plan.n_tiles) * int(self.plan.ch_per_tile)
+        buf = np.zeros(npad, RECORD_DTYPE)
+        L.check("qhtp_matmul_read_records", L.lib.qhtp_matmul_read_records(
+            C.byref(self.plan), buf.ctypes.data, buf.nbytes, _stream_handle(stream)))
+        return buf
+
+    def run_prepared(self, act: torch.Tensor, out: torch.Tensor, chain: int = 1, stream=None) -> torch.Tensor:
+        """The qhtp_<family>_run_prepared entry point (handwritten_hmx_matmul.h:46-50 counterpart)."""
+        m = act.shape[0]
+        nbytes = int(L.lib.qhtp_prepared_run_scratch_bytes(C.byref(self.plan), m, chain))
+        scratch = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        run = L.QhtpPreparedRun(
+            m=m, k=self.k, n=self.n, chain=chain,
+            activation=L.QhtpConstBuffer(_ptr(act), act.numel() * act.element_size()),
+            plan=C.pointer(self.plan),
+            scratch=L.QhtpBuffer(_ptr(scratch), nbytes),
+            output=L.QhtpBuffer(_ptr(out), out.numel() * out.element_size()),
+            stream=_stream_handle(stream))
+        fn = getattr(L.lib, f"qhtp_{self.family}_run_prepared")
+        L.check(f"qhtp_{self.family}_run_prepared", fn(C.byref(run)))
+        self._last_scratch = scratch   # keep alive until the stream is done with it
+        return out
+
+
+def lpbq_expand_i8(w4_kpair: torch.Tensor, block_scale: torch.Tensor, k: int, n: int, block: int,
+                   stream=None) -> torch.Tensor:
+    """HmxW4LpbqExpandToI8: int4 K-pair [K/2,N] x uint8 [N,K/block] -> int8 [N,K] (row-major)."""
+    out = torch.empty((n, k), dtype=torch.int8, device=w4_kpair.device)
+    L.check("qhtp_lpbq_expand_i8", L.lib.qhtp_lpbq_expand_i8(
+        _ptr(w4_kpair), _ptr(block_scale.contiguous()), k, n, block, _ptr(out), _stream_handle(stream)))
+    return out
+
+
+def _one_shot(family, act, weight, weight_scale, bias_q, act_scale, out_scale, **kw):
+    return QuantMatMul(family, weight, weight_scale, bias_q, act_scale=act_scale, out_scale=out_scale, **kw)(act)
+
+
+def hmx_u8i8_to_u8_matmul(act, weight, weight_scale, bias_q, *, act_scale, out_scale, **kw):
+    """One-shot HmxU8I8ToU8MatMul (prepare + run)."""
+    return _one_shot("u8i8", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
+
+
+def hmx_u8i4_to_u8_matmul(act, weight, weight_scale, bias_q, *, act_scale, out_scale, **kw):
+    """One-shot HmxU8I4ToU8MatMul (W4A8, per-channel or LPBQ)."""
+    return _one_shot("w4a8", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
+
+
+def hmx_u16i8_to_u16_matmul(act, weight, weight_scale, bias_q, *, act_scale, out_scale, **kw):
+    """One-shot HmxU16I8ToU16MatMul (W8A16)."""
+    return _one_shot("w8a16", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
+
+
+def hmx_u16i4_to_u16_matmul(act, weight, weight_scale, bias_q, *, act_scale, out_scale, **kw):
+    """One-shot HmxU16I4ToU16MatMul (W4A16, per-channel or LPBQ)."""
+    return _one_shot("w4a16", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
+
+
+def hmx_u16i16_to_u16_matmul(act, weight, weight_scale, bias_q, *, act_scale, out_scale, **kw):
+    """One-shot HmxU16I16ToU16MatMul (W16A16 as two byte-weight passes)."""
+    return _one_shot("w16a16", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
+
+
+def requant_code_host(T: int, c: float, mul: int, e2: int, act_mant: int, out_mant: int, out_exp2: int,
+                      zp_out: int, qmax: int) -> int:
+    """The kernels' exact requant decision, evaluated on the host (testing aid)."""
+    return int(L.lib.qhtp_requant_code_host(T, c, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax))
