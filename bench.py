@@ -1,0 +1,428 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized-MatMul hot path (and the GDN chunk inverse) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemm|gdn]
+
+Headline workload: W4A16 LPBQ GEMM, M=4096, K=4096, N=14336, LPBQ block 64, u16
+activations from N(0,1), int4 weights from N(0,0.02), int32 bias, u16 output.  A "step" is one
+quantized GEMM over one batch of synthetic input.  Metric: logical TOPS = 2*M*N*K / step time.
+
+Multi-GPU (torchrun): the GEMM shards over N -- every rank owns a 14336-wide slab of output
+channels (its own weights), so per-GPU work is fixed ("weak" scaling) and no collective touches
+the data path; ``--allgather`` additionally gathers the outputs with NCCL and reports that time
+separately.  Timing: CUDA events on the launching stream, per step, L2 flushed between steps,
+max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ----------------------------------------------------------------------------------------------
+# synthetic inputs (generated on the device; BASELINE.json distributions)
+# ----------------------------------------------------------------------------------------------
+def synth_w4a16_lpbq(m: int, k: int, n: int, block: int, seed: int, device) -> dict:
+    """u16 activations (asymmetric, fixed zp 32768) and LPBQ int4 weights, quantized with the
+    reference generator's rules: symmetric int4 per (channel, K-block) group scales, factorised as
+    per-channel base x integer factor in [1,16] (generate_qnn_matmul_python_cases.py:189-200,320-361)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn((m, k), generator=g, device=device)
+    w = torch.randn((n, k), generator=g, device=device) * 0.02
+    b = torch.randn((n,), generator=g, device=device) * 0.1
+    s_a = max(-float(x.min()) / 32768.0, float(x.max()) / 32767.0, 1e-12)
+    act = torch.clamp(torch.round(x.double() / s_a + 32768), 0, 65535).to(torch.int32).to(torch.uint16)
+    wb = w.double().reshape(n, k // block, block)
+    gs = (wb.abs().amax(dim=2).clamp_min(1e-12) / 7.0).float().double()
+    base = torch.maximum(gs.amin(dim=1).clamp_min(1e-12), gs.amax(dim=1).clamp_min(1e-12) / 16.0)
+    f = torch.clamp(torch.ceil(gs / base[:, None] - 1e-9), 1, 16)
+    q = torch.clamp(torch.round(wb / (base[:, None, None] * f[:, :, None])), -7, 7).to(torch.int8).reshape(n, k)
+    scale = base.float()
+    bias_q = torch.clamp(torch.round(b.double() / (s_a * scale.double())), -2 ** 31, 2 ** 31 - 1).to(torch.int32)
+    # output scale from the float output of the first 256 rows
+    y = x[:256].double() @ w.double().t() + b.double()
+    s_o = max(-float(y.min()) / 32768.0, float(y.max()) / 32767.0, 1e-12)
+    nib = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).t().contiguous()
+    return dict(act=act, w_packed=packed, q=q, factor=f.to(torch.uint8).contiguous(), scale=scale.contiguous(),
+                bias_q=bias_q.contiguous(), s_a=s_a, s_o=s_o, m=m, k=k, n=n, block=block)
+
+
+def synth_gdn_A(n_chunks: int, C: int, dk: int, seed: int, device) -> torch.Tensor:
+    """A = -strict_tril(beta_i (k_i.k_j) exp(g_i - g_j)), k L2-normalised, beta = sigmoid(N(0,1)),
+    g = cumsum(logsigmoid(0.5 N(0,1) - 2)) per chunk; bf16 (BASELINE.json GDN config)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = torch.empty((n_chunks, C, C), dtype=torch.bfloat16, device=device)
+    tril = torch.tril(torch.ones(C, C, dtype=torch.bool, device=device), -1)
+    for s in range(0, n_chunks, 256):
+        e = min(n_chunks, s + 256)
+        kk = torch.randn((e - s, C, dk), generator=g, device=device)
+        kk = kk / torch.sqrt((kk * kk).sum(-1, keepdim=True) + 1e-6)
+        beta = torch.sigmoid(torch.randn((e - s, C), generator=g, device=device))
+        gg = torch.cumsum(torch.nn.functional.logsigmoid(0.5 * torch.randn((e - s, C), generator=g, device=device)
+                                                         - 2.0), dim=-1)
+        diff = gg[:, :, None] - gg[:, None, :]
+        A = -(beta[:, :, None] * (kk @ kk.transpose(1, 2)) * torch.exp(torch.where(tril, diff, -torch.inf)))
+        out[s:e] = torch.where(tril, A, 0.0).to(torch.bfloat16)
+    return out
+
+
+# ----------------------------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.samples = []
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append(parts)
+
+    def summary(self) -> dict:
+        if not getattr(self, "samples", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(p[0]) for p in self.samples if p[0].replace(".", "").isdigit()]
+        mx = [float(p[1]) for p in self.samples if p[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in self.samples for i in range(4) if p[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------------------------
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, stream) -> list[float]:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.add_(1)                      # evict L2 (256 MB write) outside the timed window
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e-3)
+    torch.cuda.synchronize()
+    barrier(world)
+    return times
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline: the reference's float64 oracle path (quantize_case core), on a row sample
+# ----------------------------------------------------------------------------------------------
+def cpu_gemm_baseline(d: dict, budget_s: float = 12.0) -> dict:
+    from oracle import mm_oracle as O   # the checker; timed here as the reference CPU implementation
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"),
+                      default=os.cpu_count())
+    except Exception:
+        threads = os.cpu_count()
+    k, n = d["k"], d["n"]
+    q = d["q"].cpu().numpy()
+    f = d["factor"].cpu().numpy()
+    scale = d["scale"].cpu().numpy()
+    expanded = (q.astype(np.int16).reshape(n, k // d["block"], d["block"]) *
+                f.astype(np.int16)[:, :, None]).reshape(n, k)
+    w_deq = (expanded.astype(np.float32) * scale[:, None]).astype(np.float64)   # prepared once
+    bias_deq = d["bias_q"].cpu().numpy().astype(np.float64) * (d["s_a"] * scale.astype(np.float64))
+    act = d["act"].cpu().numpy()
+    rows, elapsed = 8, 0.0
+    while True:
+        xs = act[:rows]
+        t0 = time.perf_counter()
+        x_deq = (xs.astype(np.float64) - 32768) * d["s_a"]
+        y = x_deq @ w_deq.T + bias_deq
+        O.quantize_affine(y, d["s_o"], -32768, 65535, np.uint16)
+        elapsed = time.perf_counter() - t0
+        if elapsed * 2 > budget_s or rows * 2 > act.shape[0]:
+            break
+        rows *= 2
+    tops = 2.0 * rows * n * k / elapsed / 1e12
+    return {"value": tops, "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
+            "sample": f"{rows} of {act.shape[0]} rows, full K={k}, N={n}: float64 x_deq @ w_deq.T + bias, "
+                      f"requant (generate_qnn_matmul_python_cases.py:472-481 restated); {elapsed:.2f} s",
+            "seconds": elapsed}
+
+
+def cpu_gdn_baseline(A: torch.Tensor, budget_s: float = 10.0) -> dict:
+    from oracle import gdn_oracle as G
+    import ctypes
+    lib_path = ROOT / "oracle" / "libgdn_block_ref.so"
+    a = A.float().cpu().numpy()
+    C = a.shape[-1]
+    threads = os.cpu_count()
+    n, el = 4, 0.0
+    while True:
+        sub = a[:n]
+        sA = float(np.abs(sub).max() / 32767.0)
+        Aq = np.clip(np.rint(sub / sA), -32767, 32767).astype(np.int16)
+        T = np.zeros(sub.shape, np.float64)
+        sAv = np.full(n, sA, np.float32)
+        t0 = time.perf_counter()
+        if lib_path.exists():
+            lib = ctypes.CDLL(str(lib_path))
+            lib.gdn_block_ref_solve(Aq.ctypes.data_as(ctypes.c_void_p), sAv.ctypes.data_as(ctypes.c_void_p),
+                                    ctypes.c_float(2.0 / 32767.0), n, C, T.ctypes.data_as(ctypes.c_void_p),
+                                    threads)
+            kind = "port"
+        else:
+            G.inverse_fp64(sub)
+            kind = "port"
+        el = time.perf_counter() - t0
+        if el * 2 > budget_s or n * 2 > a.shape[0]:
+            break
+        n *= 2
+    return {"value": n / el, "unit": "chunks/s", "cores": threads, "kind": kind,
+            "sample": f"{n} chunks of C={C}: BL=16 int16-code forward substitution + fp64 block merge "
+                      f"(gdn_solve_ref.c restated, OpenMP over chunks); {el:.2f} s"}
+
+
+# ----------------------------------------------------------------------------------------------
+# workloads
+# ----------------------------------------------------------------------------------------------
+def run_gemm(args, world, rank, local, stream) -> dict:
+    from qcom_htp_b200 import QuantMatMul
+    dev = torch.device("cuda", local)
+    m, k, n, blk = args.m, args.k, args.n, 64
+    d = synth_w4a16_lpbq(m, k, n, blk, seed=1234 + rank, device=dev)
+    op = QuantMatMul("w4a16", d["w_packed"], d["scale"], d["bias_q"], act_scale=d["s_a"], out_scale=d["s_o"],
+                     schema="lpbq", lpbq_block_scale=d["factor"], lpbq_block=blk)
+    act, out = d["act"], torch.empty((m, n), dtype=torch.uint16, device=dev)
+    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    fn = lambda: op(act, out)
+    with ClockSampler(local) as clk:
+        times = timed_steps(fn, args.steps, args.warmup, flush, world, stream)
+    op.check_device(m)
+    t_step = max_over_ranks(statistics.mean(times), world)
+    ops = 2.0 * m * n * k
+    value = ops * world / t_step / 1e12
+    # end to end through the public API with host buffers: pinned H2D of the activation, GEMM,
+    # D2H of the output, every step
+    act_h = act.cpu().pin_memory()
+    out_h = torch.empty((m, n), dtype=torch.uint16).pin_memory()
+    act_d = torch.empty_like(act)
+
+    def e2e():
+        act_d.copy_(act_h, non_blocking=True)
+        op(act_d, out)
+        out_h.copy_(out, non_blocking=True)
+
+    t_e2e = max_over_ranks(statistics.mean(timed_steps(e2e, max(3, args.steps // 2), 2, flush, world, stream)),
+                           world)
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]      # dense int8 rate is 2x dense bf16 on B200
+    achieved = ops / statistics.mean(times) / 1e12
+    executed = achieved * 4                   # 2 activation byte planes x (q, e') weight planes
+    res = {
+        "metric": "w4a16_lpbq_gemm_tops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u16xint4->u16 (int8 tensor ops, int64 combine)",
+        "data": "synthetic (BASELINE.json distributions, generated on device)",
+        "config": {"workload": "W4A16 LPBQ GEMM (BASELINE configs[2]/[4] shape)", "m": m, "k": k,
+                   "n_per_gpu": n, "lpbq_block": blk, "parallelism": f"N-shard x{world}, no data-path collective",
+                   "l2": "256 MB write between steps (flush)", "bit_exact": True},
+        "e2e": {"value": ops * world / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
+                "d2h_bytes_per_step": m * n * 2},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / int8_peak, "traffic": None, "op_kind": "int8 MAC x2, logical",
+                     "executed_tflops": executed, "frac_executed": executed / int8_peak,
+                     "peak_src": f"2 x bf16_tflops ({pk['src']}, burst)",
+                     "kernel": "split_u16_planes + qgemm_kernel<2,F32> (one qhtp_matmul_run)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if args.allgather and world > 1:
+        import torch.distributed as dist
+        gathered = torch.empty((world, m, n), dtype=torch.uint16, device=dev)
+        ag = lambda: dist.all_gather_into_tensor(gathered.view(torch.int16), out.view(torch.int16))
+        t_ag = max_over_ranks(statistics.mean(timed_steps(ag, max(3, args.steps // 2), 2, flush, world, stream)),
+                              world)
+        res["allgather"] = {"ms": t_ag * 1e3, "bytes": world * m * n * 2,
+                            "tops_incl_allgather": ops * world / (t_step + t_ag) / 1e12}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_gemm_baseline(d)
+    if not args.no_gdn:
+        res["secondary"] = run_gdn(args, world, rank, local, stream, secondary=True)
+    return res
+
+
+def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
+    from qcom_htp_b200 import gdn_inverse
+    dev = torch.device("cuda", local)
+    C = 256
+    n_chunks = args.gdn_chunks
+    A = synth_gdn_A(n_chunks, C, 128, seed=99 + rank, device=dev)
+    T = torch.empty((n_chunks, C, C), dtype=torch.float32, device=dev)
+    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    fn = lambda: gdn_inverse(A, T)
+    steps = args.steps
+    with ClockSampler(local) as clk:
+        times = timed_steps(fn, steps, args.warmup, flush, world, stream)
+    t = max_over_ranks(statistics.mean(times), world)
+    pk = peaks()
+    bytes_alg = n_chunks * (C * C * 2 + C * C * 4)       # read A (bf16), write T (fp32)
+    achieved = bytes_alg / statistics.mean(times) / 1e9
+    res = {"metric": "gdn_inverse_chunks_per_s", "value": n_chunks * world / t, "unit": "chunks/s",
+           "ms_per_step": t * 1e3, "config": {"workload": "GDN C=256 inverse", "chunks_per_gpu": n_chunks,
+                                             "note": "batch 8 x 32 heads x 16 chunks per GPU"},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                        "peak_src": f"hbm_gbs ({pk['src']})"},
+           "gpu_launches": steps, "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_gdn_baseline(A)
+    if not secondary:
+        res.update({"n_gpus": world, "steps": steps, "warmup": args.warmup, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in / fp32 out (tf: bf16 MMA, fp32 acc)",
+                    "data": "synthetic (BASELINE.json GDN distribution, generated on device)",
+                    "e2e": None})
+    return res
+
+
+# ----------------------------------------------------------------------------------------------
+# reference arm: the reference's own CPU implementation of the path, on the host cores
+# ----------------------------------------------------------------------------------------------
+def run_reference(args, world, rank) -> None:
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    m, k, n = args.m, args.k, args.n
+    d = synth_w4a16_lpbq(m, k, n, 64, seed=1234, device=dev)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_gemm_baseline(d, budget_s=max(2.0, 60.0 / max(1, args.steps + args.warmup)))
+        if i >= args.warmup:
+            vals.append(r)
+    v = statistics.mean(x["value"] for x in vals)
+    out = {"impl": "reference", "metric": "w4a16_lpbq_gemm_tops", "value": v, "unit": "TFLOP/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "config": {"workload": "W4A16 LPBQ GEMM (BASELINE configs[2]/[4] shape)", "m": m, "k": k, "n_per_gpu": n,
+                      "lpbq_block": 64},
+           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": vals[-1]["cores"], "kind": "port",
+                            "sample": vals[-1]["sample"]},
+           "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference has no GPU path; its CPU oracle (float64 numpy) is timed on the host cores"}
+    print(json.dumps(out))
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gemm", "gdn"], default="gemm")
+    ap.add_argument("--m", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--n", type=int, default=14336)
+    ap.add_argument("--gdn-chunks", type=int, default=4096)
+    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--no-gdn", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        # rank 0 alone times the CPU implementation; other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return 0
+    world, rank, local = dist_init()
+    stream = torch.cuda.current_stream()
+    res = run_gemm(args, world, rank, local, stream) if args.workload == "gemm" else \
+        run_gdn(args, world, rank, local, stream)
+    if rank == 0:
+        print(json.dumps(res))
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
