@@ -409,8 +409,8 @@ def make_baseline_case(family: str, m: int, k: int, n: int, seed: int = 0x6D6D,
 # 3. Prepared record ("sidecar") and the exact requant model
 # ----------------------------------------------------------------------------------------------
 
-RECORD_DTYPE = np.dtype([("beff", "<i8"), ("c", "<f8"), ("m_q", "<i4"), ("mul", "<u4"),
-                         ("e2", "<i4"), ("pad", "<i4")])   # 32 bytes / output channel
+RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cm", "<u8"), ("m_q", "<i4"), ("mul", "<u4"),
+                         ("e2", "<i2"), ("cshift", "<i2"), ("pad", "<i4")])   # 32 bytes / output channel
 
 
 def split_f32(scale: np.ndarray):
@@ -455,7 +455,9 @@ def prepare_record(case: QuantCase, dequant: str = "f32") -> tuple[np.ndarray, n
     beff  : effective bias in T units.  f32 mode: m_s*(bias_q - zp*sum q) - zp*sum e';
             exact mode: bias_q - zp*sum q   (docs/qnn_custom_op_matmul_e2e.md:345-355 folds the
             activation zero-point into the bias the same way: bias_q - zp_act*sum_k w)
-    c     : float64 multiplier, z ~= T*c + zp_out   (fast path)
+    cm, cshift : the float64 requant multiplier c = cm * 2**-cshift (cm its 53-bit integer
+            mantissa), c = float64(s_A*2**e_s / s_O) in f32 mode, float64(float64(s_A*s_W)/s_O) in
+            exact mode; fast path z ~= T*c + zp_out evaluated exactly in fixed point (T*cm)
     m_q   : multiplier of the q-plane accumulator inside T (m_s in f32 mode, 1 in exact mode)
     mul   : extra integer factor of T in the exact tie check (1 in f32 mode, m_s in exact mode)
     e2    : binary exponent so that  z* - zp_out = T*mul*mant(s_A)*2**e2 / s_O
@@ -475,20 +477,27 @@ def prepare_record(case: QuantCase, dequant: str = "f32") -> tuple[np.ndarray, n
         ep = residual_plane(wq, m_s)
         sum_e = ep.astype(np.int64).sum(axis=1)
         rec["beff"] = m_s * (bias - zp * sum_q) - zp * sum_e
-        rec["c"] = np.ldexp(np.float64(case.act_scale), e_s) / np.float64(case.out_scale)
+        c = np.ldexp(np.float64(case.act_scale), e_s) / np.float64(case.out_scale)
         rec["m_q"] = m_s
         rec["mul"] = 1
     elif dequant == "exact":
         ep = None
         rec["beff"] = bias - zp * sum_q
-        rec["c"] = (np.float64(case.act_scale) * case.weight_scale.astype(np.float64)) / np.float64(
-            case.out_scale)
+        c = (np.float64(case.act_scale) * case.weight_scale.astype(np.float64)) / np.float64(case.out_scale)
         rec["m_q"] = 1
         rec["mul"] = m_s
     else:
         raise ValueError(dequant)
+    fc, ec = np.frexp(c)
+    rec["cm"] = np.ldexp(fc, 53).astype(np.uint64)
+    rec["cshift"] = 53 - ec
     rec["e2"] = e_s + ea_m
     return rec, ep
+
+
+def record_c(rec: np.ndarray) -> np.ndarray:
+    """float64 requant multiplier c held by a record (exact: cm < 2**53)."""
+    return np.ldexp(rec["cm"].astype(np.float64), -rec["cshift"].astype(np.int64))
 
 
 def _exact_round(tpre: int, mul: int, e_s: int, s_a: float, s_o: float, zp_out: int) -> int:
@@ -512,7 +521,7 @@ def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
     tpre = rec["m_q"].astype(np.int64)[None, :] * p + rec["beff"][None, :]
     if ep is not None:
         tpre += (xq @ ep.astype(np.float64).T).astype(np.int64)
-    z = tpre.astype(np.float64) * rec["c"][None, :] + fam.out_zp
+    z = tpre.astype(np.float64) * record_c(rec)[None, :] + fam.out_zp
     r = np.rint(z)
     frac = z - np.floor(z)
     near = (np.abs(frac - 0.5) <= TIE_EPS) & (z > -1.0) & (z < fam.out_qmax + 1.0)

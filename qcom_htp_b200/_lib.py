@@ -86,8 +86,8 @@ SIGNATURES = {
     "qhtp_gdn_inverse_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     "qhtp_gdn_solve_u16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_float, C.c_int32,
                                      C.c_float, C.c_void_p, C.c_void_p]),
-    "qhtp_requant_code_host": (C.c_int32, [C.c_int64, C.c_double, C.c_uint32, C.c_int32, C.c_uint64, C.c_uint64,
-                                           C.c_int32, C.c_int32, C.c_int32]),
+    "qhtp_requant_code_host": (C.c_int32, [C.c_int64, C.c_uint64, C.c_int32, C.c_uint32, C.c_int32, C.c_uint64,
+                                           C.c_uint64, C.c_int32, C.c_int32, C.c_int32]),
 }
 
 
@@ -101,7 +101,7 @@ class QhtpError(RuntimeError):
 
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
-        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m qcom_htp_b200.build` "
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python qcom_htp_b200/build.py` "
                           "(there is no CPU fallback)")
     lib = C.CDLL(str(LIB_PATH))
     for name, (res, args) in SIGNATURES.items():

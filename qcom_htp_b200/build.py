@@ -1,6 +1,6 @@
 """Build libqhtp.so (the C-ABI library with the sm_100a kernels) in-tree with nvcc.
 
-    python -m qcom_htp_b200.build            # -> qcom_htp_b200/libqhtp.so
+    python qcom_htp_b200/build.py [--force] [--ptxas-v]   # -> qcom_htp_b200/libqhtp.so
 
 The library is compiled only for sm_100a (B200): tcgen05 / TMA / TMEM instructions are used
 directly, so there is no other target.

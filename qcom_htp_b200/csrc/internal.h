@@ -10,23 +10,27 @@ namespace qhtp {
 
 constexpr uint32_t kPlanMagic = 0x51485450u;  // "QHTP"
 
-// Kernel variants of the quantized GEMM.
+// Kernel variants of the quantized GEMM.  Every tile covers 128 output rows x 128 output channels.
 enum GemmMode : uint32_t {
   kModeF32 = 0,    // f32 weight dequant: B tile = [q (128 ch) | e' (128 ch)], s8
-  kModeExact = 1,  // exact dequant, 8-bit weights: B tile = q (256 ch), s8
+  kModeExact = 1,  // exact dequant, 8-bit weights: B tile = q (128 ch), s8
   kModeW16 = 2,    // exact dequant, int16 weights: B tile = [hi s8 (128 ch) | lo u8 (128 ch)]
 };
 
 constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
-constexpr int kTileBRows = 256;  // weight-plane rows per tile
+constexpr int kTileN = 128;      // output channels per tile
 constexpr int kTileK = 128;      // bytes of K per pipeline stage (one 128-byte swizzle row)
+
+// weight-plane rows per tile in the prepared layout
+inline constexpr uint32_t b_rows_for_mode(uint32_t mode) { return mode == kModeExact ? 128u : 256u; }
 
 struct ChannelRecord {  // 32 bytes, one per output channel (padded to the tile)
   int64_t beff;         // effective bias, in accumulator units
-  double c;             // fast-path multiplier: z ~= T * c + zp_out
+  uint64_t cm;          // requant multiplier c = cm * 2^-cshift (cm: 53-bit mantissa of the float64 c)
   int32_t m_q;          // multiplier of the q-plane accumulator inside T
   uint32_t mul;         // extra factor of T in the exact tie check
-  int32_t e2;           // binary exponent of the exact tie check
+  int16_t e2;           // binary exponent of the exact tie check
+  int16_t cshift;
   int32_t pad;
 };
 static_assert(sizeof(ChannelRecord) == 32, "record layout");

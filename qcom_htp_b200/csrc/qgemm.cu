@@ -1,5 +1,5 @@
-// Quantized MatMul family on B200: tcgen05 kind::i8 GEMM with TMEM accumulators, TMA-staged
-// 128-byte-swizzled shared-memory tiles, and a fused exact requant epilogue.
+// Quantized MatMul family on B200: persistent tcgen05 kind::i8 GEMM with TMEM accumulators,
+// TMA-staged 128-byte-swizzled shared-memory tiles, and a fused exact requant epilogue.
 //
 // Mapping of the reference arithmetic (scripts/generate_qnn_matmul_python_cases.py:426-481) onto
 // integer tensor-core products:
@@ -12,8 +12,13 @@
 //     tile is [q rows | e' rows]: one N=256 MMA yields both sum(x*q) and sum(x*e').
 //   * int16 weights (W16A16) are two byte planes, hi (s8) and lo (u8) (verify_w16a16_two_w8a16.py:21-48),
 //     giving three accumulators (hi*hi, hi*lo+lo*hi, lo*lo) combined with x65536 / x256 / x1.
-// CTA roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
-// warps 2..5 = epilogue (TMEM -> registers -> int64 combine -> exact requant -> global).
+//
+// Persistent CTAs (one per SM) walk 128x128 output tiles.  Roles (320 threads):
+//   warp 0      TMA producer (one lane): activation plane(s) + weight planes per 128-byte K step
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2..9  epilogue: each thread owns one output row and 64 channels; it drains the TMEM
+//               accumulators into int64 registers, releases TMEM (the next tile's MMAs start),
+//               then requantizes from registers with integer fixed-point math and stores.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -61,11 +66,22 @@ bool make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   return r == CUDA_SUCCESS;
 }
 
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 // ------------------------------------------------------------------------------------------------
 // GEMM kernel
 // ------------------------------------------------------------------------------------------------
 struct GemmParams {
-  int M, N, kblocks, a_plane_rows, ch_per_tile;
+  int M, N, m_tiles, n_tiles, kblocks, a_plane_rows;
   const ChannelRecord* rec;
   void* out;
   int zp_out, qmax;
@@ -74,53 +90,70 @@ struct GemmParams {
   int* err;
 };
 
-template <int PA>
-struct GemmCfg {
-  static constexpr int kStageA = kTileM * kTileK;        // 16 KB per activation plane
-  static constexpr int kStageB = kTileBRows * kTileK;    // 32 KB of weight planes
-  static constexpr int kStage = PA * kStageA + kStageB;
-  static constexpr int kStages = (PA == 1) ? 4 : 3;
-  static constexpr int kRecBytes = 256 * sizeof(ChannelRecord);
-  static constexpr int kSmem = kStages * kStage + kRecBytes + 256 + 1024;
-};
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 template <int PA, int MODE>
-__global__ void __launch_bounds__(192, 1)
+struct GemmCfg {
+  static constexpr int kBRows = MODE == kModeExact ? 128 : 256;
+  static constexpr int kStageA = kTileM * kTileK;  // 16 KB per activation plane
+  static constexpr int kStageB = kBRows * kTileK;  // weight planes
+  static constexpr int kStage = PA * kStageA + kStageB;
+  static constexpr int kStagesRaw = (200 * 1024) / kStage;
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kSmem = kStages * kStage + 1024 + 256;
+};
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void load_record(const ChannelRecord* rec, ChannelRecord& r) {
+  const uint4* p = reinterpret_cast<const uint4*>(rec);
+  const uint4 a = __ldg(p), b = __ldg(p + 1);
+  r.beff = static_cast<int64_t>((static_cast<uint64_t>(a.y) << 32) | a.x);
+  r.cm = (static_cast<uint64_t>(a.w) << 32) | a.z;
+  r.m_q = static_cast<int32_t>(b.x);
+  r.mul = b.y;
+  r.e2 = static_cast<int16_t>(b.z & 0xFFFFu);
+  r.cshift = static_cast<int16_t>(b.z >> 16);
+}
+
+template <int PA, int MODE>
+// 320 threads x 200 registers = 64000 <= 65536: the epilogue keeps 64 int64 accumulators in registers.
+__global__ void __maxnreg__(200)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-  using Cfg = GemmCfg<PA>;
+  using Cfg = GemmCfg<PA, MODE>;
   constexpr int S = Cfg::kStages;
-  constexpr uint32_t kTmemCols = (PA == 2 || MODE == kModeW16) ? 512 : 256;
+  constexpr uint32_t kTmemCols = 512;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  ChannelRecord* srec = reinterpret_cast<ChannelRecord*>(smem + S * Cfg::kStage);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage + Cfg::kRecBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
   uint64_t* empty = full + S;
-  uint64_t* accf = empty + S;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTileM;
-  const int tile_n = blockIdx.y;
+  const int total_tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    mbar_init(tfull, 1);
+    mbar_init(tempty, kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 1) {
     tmem_alloc(tslot, kTmemCols);
     tmem_relinquish();
-  }
-  if (warp >= 2) {  // stage this tile's channel records in shared memory
-    const uint4* src = reinterpret_cast<const uint4*>(p.rec + static_cast<size_t>(tile_n) * p.ch_per_tile);
-    uint4* dst = reinterpret_cast<uint4*>(srec);
-    for (int i = threadIdx.x - 64; i < p.ch_per_tile * 2; i += 128) dst[i] = src[i];
   }
   tc_fence_before();
   __syncthreads();
@@ -128,141 +161,161 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      for (int kb = 0; kb < p.kblocks; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], Cfg::kStage);
-        uint8_t* st = stages + s * Cfg::kStage;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % p.m_tiles) * kTileM;
+        const int nb = (tile / p.m_tiles) * Cfg::kBRows;
+        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+          uint8_t* st = stages + s * Cfg::kStage;
 #pragma unroll
-        for (int pl = 0; pl < PA; ++pl)
-          tma_load_2d(st + pl * Cfg::kStageA, &tmA, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
-        tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], kb * kTileK, tile_n * kTileBRows);
+          for (int pl = 0; pl < PA; ++pl)
+            tma_load_2d(st + pl * Cfg::kStageA, &tmA, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
+          tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], kb * kTileK, nb);
+        }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int kb = 0; kb < p.kblocks; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&full[s], ph, p.err, kErrTimeoutFull)) {
-          ok = false;
-          break;
-        }
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++tc) {
+        if (!mbar_wait(tempty, (tc & 1) ^ 1, p.err, kErrTimeoutOther)) break;
         tc_fence_after();
-        const uint32_t st = smem_u32(stages + s * Cfg::kStage);
-        const uint64_t dA0 = desc_kmajor_sw128(st);
-        const uint64_t dA1 = desc_kmajor_sw128(st + (PA > 1 ? Cfg::kStageA : 0));
-        const uint64_t dB = desc_kmajor_sw128(st + PA * Cfg::kStageA);
-#pragma unroll
-        for (int kk = 0; kk < kTileK / 32; ++kk) {
-          const uint32_t acc = (kb | kk) ? 1u : 0u;
-          const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
-          if constexpr (MODE == kModeW16) {
-            constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);  // u8 act x s8 hi-byte weight
-            constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);  // u8 act x u8 lo-byte weight
-            const uint64_t dBhi = dB + ko;
-            const uint64_t dBlo = dB + ko + (128 * kTileK >> 4);
-            mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
-            mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
-            mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
-            mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
-          } else {
-            constexpr uint32_t id = idesc_i8(128, 256, 0, 1);
-            mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
-            if constexpr (PA == 2) mma_i8(tmem + 256, dA1 + ko, dB + ko, id, acc);
+        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, p.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t st = smem_u32(stages + s * Cfg::kStage);
+          const uint64_t dA0 = desc_kmajor_sw128(st);
+          const uint64_t dA1 = desc_kmajor_sw128(st + (PA > 1 ? Cfg::kStageA : 0));
+          const uint64_t dB = desc_kmajor_sw128(st + PA * Cfg::kStageA);
+#pragma unroll
+          for (int kk = 0; kk < kTileK / 32; ++kk) {
+            const uint32_t acc = (kb | kk) ? 1u : 0u;
+            const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
+            if constexpr (MODE == kModeW16) {
+              constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);  // u8 act x s8 hi-byte weight
+              constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);  // u8 act x u8 lo-byte weight
+              const uint64_t dBhi = dB + ko;
+              const uint64_t dBlo = dB + ko + (128 * kTileK >> 4);
+              mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
+              mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
+              mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
+              mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
+            } else {
+              constexpr int N = Cfg::kBRows;  // 256 = [q | e'] (f32 mode), 128 = q (exact mode)
+              constexpr uint32_t id = idesc_i8(128, N, 0, 1);
+              mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
+              if constexpr (PA == 2) mma_i8(tmem + N, dA1 + ko, dB + ko, id, acc);
+            }
+          }
+          mma_commit(&empty[s]);  // stage free once these MMAs have read it
         }
-        mma_commit(&empty[s]);  // stage free once these MMAs have read it
+        if (ok) mma_commit(tfull);  // accumulators of this tile complete
       }
-      if (ok) mma_commit(accf);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int quad = warp & 3;
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;          // which 64 of the 128 channels
     const int row = quad * 32 + lane;
-    const int m = m0 + row;
-    const bool ready = mbar_wait(accf, 0, p.err, kErrTimeoutAccum);
-    tc_fence_after();
-    if (ready) {
-      const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-      const int n_base = tile_n * p.ch_per_tile;
-      const bool u16 = p.qmax > 255;
-      for (int c0 = 0; c0 < p.ch_per_tile; c0 += 16) {
-        uint32_t r0[16], r1[16], r2[16], r3[16];
+    const bool u16 = p.qmax > 255;
+    uint32_t tc = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
+      const int m = (tile % p.m_tiles) * kTileM + row;
+      const int n0 = (tile / p.m_tiles) * kTileN + half * 64;
+      const ChannelRecord* rec = p.rec + n0;
+      if (!mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum)) break;
+      tc_fence_after();
+      const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+      int64_t T[64];
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 8) {
+        uint32_t s0[8], s1[8], s2[8], s3[8];
         if constexpr (MODE == kModeF32) {
-          tmem_ld16(tl + c0, r0);          // sum x_hi * q   (or x * q for u8 act)
-          tmem_ld16(tl + 128 + c0, r1);    // sum x_hi * e'
+          tmem_ld8(tl + c0, s0);             // sum x(_hi) * q
+          tmem_ld8(tl + 128 + c0, s1);       // sum x(_hi) * e'
           if constexpr (PA == 2) {
-            tmem_ld16(tl + 256 + c0, r2);  // sum x_lo * q
-            tmem_ld16(tl + 384 + c0, r3);  // sum x_lo * e'
+            tmem_ld8(tl + 256 + c0, s2);     // sum x_lo * q
+            tmem_ld8(tl + 384 + c0, s3);     // sum x_lo * e'
           }
         } else if constexpr (MODE == kModeExact) {
-          tmem_ld16(tl + c0, r0);
-          if constexpr (PA == 2) tmem_ld16(tl + 256 + c0, r2);
+          tmem_ld8(tl + c0, s0);
+          if constexpr (PA == 2) tmem_ld8(tl + 128 + c0, s2);
         } else {
-          tmem_ld16(tl + c0, r0);          // hi x hi
-          tmem_ld16(tl + 128 + c0, r1);    // hi x lo + lo x hi
-          tmem_ld16(tl + 256 + c0, r2);    // lo x lo
+          tmem_ld8(tl + c0, s0);             // hi x hi
+          tmem_ld8(tl + 128 + c0, s1);       // hi x lo + lo x hi
+          tmem_ld8(tl + 256 + c0, s2);       // lo x lo
         }
         tmem_ld_wait();
-        int32_t code[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const ChannelRecord& rc = srec[c0 + j];
-          int64_t T;
+        for (int j = 0; j < 8; ++j) {
+          const int64_t beff = __ldg(&rec[c0 + j].beff);
           if constexpr (MODE == kModeF32) {
-            int64_t pq = static_cast<int32_t>(r0[j]);
-            int64_t pe = static_cast<int32_t>(r1[j]);
+            const int64_t mq = __ldg(&rec[c0 + j].m_q);
+            int64_t pq = static_cast<int32_t>(s0[j]);
+            int64_t pe = static_cast<int32_t>(s1[j]);
             if constexpr (PA == 2) {
-              pq = pq * 256 + static_cast<int32_t>(r2[j]);
-              pe = pe * 256 + static_cast<int32_t>(r3[j]);
+              pq = pq * 256 + static_cast<int32_t>(s2[j]);
+              pe = pe * 256 + static_cast<int32_t>(s3[j]);
             }
-            T = static_cast<int64_t>(rc.m_q) * pq + pe + rc.beff;
+            T[c0 + j] = mq * pq + pe + beff;
           } else if constexpr (MODE == kModeExact) {
-            int64_t pq = static_cast<int32_t>(r0[j]);
-            if constexpr (PA == 2) pq = pq * 256 + static_cast<int32_t>(r2[j]);
-            T = pq + rc.beff;
+            int64_t pq = static_cast<int32_t>(s0[j]);
+            if constexpr (PA == 2) pq = pq * 256 + static_cast<int32_t>(s2[j]);
+            T[c0 + j] = pq + beff;
           } else {
-            T = static_cast<int64_t>(static_cast<int32_t>(r0[j])) * 65536 +
-                static_cast<int64_t>(static_cast<int32_t>(r1[j])) * 256 + static_cast<int32_t>(r2[j]) + rc.beff;
+            T[c0 + j] = static_cast<int64_t>(static_cast<int32_t>(s0[j])) * 65536 +
+                        static_cast<int64_t>(static_cast<int32_t>(s1[j])) * 256 + static_cast<int32_t>(s2[j]) + beff;
           }
-          code[j] = requant_code(T, rc.c, rc.mul, rc.e2, p.act_mant, p.out_mant, p.out_exp2, p.zp_out, p.qmax);
         }
-        const int n = n_base + c0;
-        if (m < p.M && n < p.N) {
-          if (!u16) {
-            uint8_t* o = reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n;
-            if (n + 16 <= p.N) {
-              uint4 v;
-              v.x = (code[0] & 0xFF) | ((code[1] & 0xFF) << 8) | ((code[2] & 0xFF) << 16) | (code[3] << 24);
-              v.y = (code[4] & 0xFF) | ((code[5] & 0xFF) << 8) | ((code[6] & 0xFF) << 16) | (code[7] << 24);
-              v.z = (code[8] & 0xFF) | ((code[9] & 0xFF) << 8) | ((code[10] & 0xFF) << 16) | (code[11] << 24);
-              v.w = (code[12] & 0xFF) | ((code[13] & 0xFF) << 8) | ((code[14] & 0xFF) << 16) | (code[15] << 24);
-              *reinterpret_cast<uint4*>(o) = v;
-            } else {
-              for (int j = 0; j < 16 && n + j < p.N; ++j) o[j] = static_cast<uint8_t>(code[j]);
+      }
+      // accumulators are in registers: hand TMEM back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty);
+      if (m < p.M) {
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 8) {
+          const int n = n0 + c0;
+          if (n + 8 <= p.N) {  // channels past N (tile padding) have no record: skip them
+            uint32_t code[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              ChannelRecord r;
+              load_record(rec + c0 + j, r);
+              code[j] = static_cast<uint32_t>(requant_code(T[c0 + j], r.cm, r.cshift, r.mul, r.e2, p.act_mant,
+                                                           p.out_mant, p.out_exp2, p.zp_out, p.qmax));
             }
-          } else {
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n;
-            if (n + 16 <= p.N) {
-              uint4 v0, v1;
-              v0.x = code[0] | (code[1] << 16);
-              v0.y = code[2] | (code[3] << 16);
-              v0.z = code[4] | (code[5] << 16);
-              v0.w = code[6] | (code[7] << 16);
-              v1.x = code[8] | (code[9] << 16);
-              v1.y = code[10] | (code[11] << 16);
-              v1.z = code[12] | (code[13] << 16);
-              v1.w = code[14] | (code[15] << 16);
-              reinterpret_cast<uint4*>(o)[0] = v0;
-              reinterpret_cast<uint4*>(o)[1] = v1;
+            if (u16) {
+              uint4 v;
+              v.x = code[0] | (code[1] << 16);
+              v.y = code[2] | (code[3] << 16);
+              v.z = code[4] | (code[5] << 16);
+              v.w = code[6] | (code[7] << 16);
+              *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n) = v;
             } else {
-              for (int j = 0; j < 16 && n + j < p.N; ++j) o[j] = static_cast<uint16_t>(code[j]);
+              uint2 v;
+              v.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
+              v.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
+              *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n) = v;
             }
           }
         }
@@ -304,7 +357,7 @@ __global__ void split_u16_planes(const uint16_t* __restrict__ act, uint8_t* __re
 template <int PA, int MODE>
 static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, const CUtensorMap& tb,
                                   const GemmParams& prm) {
-  using Cfg = GemmCfg<PA>;
+  using Cfg = GemmCfg<PA, MODE>;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<PA, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -312,8 +365,9 @@ static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, co
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  dim3 grid((g.m + kTileM - 1) / kTileM, g.plan->n_tiles);
-  qgemm_kernel<PA, MODE><<<grid, 192, Cfg::kSmem, g.stream>>>(ta, tb, prm);
+  const int total = prm.m_tiles * prm.n_tiles;
+  const int grid = total < sm_count() ? total : sm_count();
+  qgemm_kernel<PA, MODE><<<grid, kGemmThreads, Cfg::kSmem, g.stream>>>(ta, tb, prm);
   return cudaGetLastError();
 }
 
@@ -327,7 +381,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
     const size_t total = static_cast<size_t>(g.m) * K;
     const size_t n8 = total / 8;
     int blocks = static_cast<int>((n8 + 255) / 256);
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
     if (blocks < 1) blocks = 1;
     split_u16_planes<<<blocks, 256, 0, g.stream>>>(static_cast<const uint16_t*>(g.act), g.planes,
                                                    g.planes + total, n8);
@@ -340,16 +394,18 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
     a_rows = g.m;
   }
   if (!make_tmap_2d_u8(&ta, a_base, K, a_rows, K, kTileK, kTileM)) return cudaErrorInvalidValue;
+  const uint32_t brows = b_rows_for_mode(pl->mode);
   const uint8_t* planes = static_cast<const uint8_t*>(pl->prepared);
-  if (!make_tmap_2d_u8(&tb, planes, pl->k_pad, static_cast<uint64_t>(pl->n_tiles) * kTileBRows, pl->k_pad, kTileK,
-                       kTileBRows))
+  if (!make_tmap_2d_u8(&tb, planes, pl->k_pad, static_cast<uint64_t>(pl->n_tiles) * brows, pl->k_pad, kTileK,
+                       brows))
     return cudaErrorInvalidValue;
   GemmParams prm;
   prm.M = static_cast<int>(g.m);
   prm.N = static_cast<int>(pl->n);
+  prm.m_tiles = static_cast<int>((g.m + kTileM - 1) / kTileM);
+  prm.n_tiles = static_cast<int>(pl->n_tiles);
   prm.kblocks = static_cast<int>(pl->k_pad / kTileK);
   prm.a_plane_rows = static_cast<int>(g.m);
-  prm.ch_per_tile = static_cast<int>(pl->ch_per_tile);
   prm.rec = reinterpret_cast<const ChannelRecord*>(planes + pl->plane_bytes);
   prm.out = g.out;
   prm.zp_out = pl->out_zp;
@@ -372,7 +428,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
 // Prepare: weight byte planes + per-channel records
 // ------------------------------------------------------------------------------------------------
 struct PrepParams {
-  uint32_t family, schema, mode, K, N, k_pad, ch_per_tile, lpbq_block;
+  uint32_t family, schema, mode, K, N, k_pad, b_rows, lpbq_block;
   const void* weight;
   const uint8_t* lpbq;
   int8_t* planes;
@@ -405,14 +461,14 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const uint32_t n = static_cast<uint32_t>(idx / chunks);
     const uint32_t k0 = static_cast<uint32_t>(idx % chunks) * 16;
-    const uint32_t tile = n / p.ch_per_tile;
-    const size_t row = static_cast<size_t>(tile) * kTileBRows + (n % p.ch_per_tile);
+    const uint32_t tile = n / kTileN;
+    const size_t row = static_cast<size_t>(tile) * p.b_rows + (n % kTileN);
     int8_t* r0 = p.planes + row * p.k_pad + k0;
+    int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;  // second plane (f32 / W16 modes)
     long long sq = 0, se = 0;
     if (p.mode == kModeF32) {
       const uint32_t bits = __float_as_uint(scale[n]);
       const int32_t ms = static_cast<int32_t>((bits & 0x7FFFFFu) | 0x800000u);
-      int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;
 #pragma unroll 4
       for (int j = 0; j < 16; ++j) {
         const int q = load_weight(p, n, k0 + j);
@@ -432,12 +488,11 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
         sq += q;
       }
     } else {
-      int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;
 #pragma unroll 4
       for (int j = 0; j < 16; ++j) {
         const int q = load_weight(p, n, k0 + j);
-        r0[j] = static_cast<int8_t>(q >> 8);                  // arithmetic high byte, s8
-        r1[j] = static_cast<int8_t>(static_cast<uint8_t>(q & 0xFF));  // low byte, u8 carrier
+        r0[j] = static_cast<int8_t>(q >> 8);                           // arithmetic high byte, s8
+        r1[j] = static_cast<int8_t>(static_cast<uint8_t>(q & 0xFF));   // low byte, u8 carrier
         sq += q;
       }
     }
@@ -460,10 +515,11 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
   if ((bits >> 31) != 0 || ex == 0 || ex == 0xFF) {  // negative, zero/subnormal, inf/nan
     atomicCAS(bad_scale, 0, 1);
     r.beff = 0;
-    r.c = 0.0;
+    r.cm = 0;
     r.m_q = 0;
     r.mul = 0;
     r.e2 = 0;
+    r.cshift = 0;
     rec[n] = r;
     return;
   }
@@ -471,25 +527,33 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
   const int es = static_cast<int>(ex) - 150;
   const int64_t sq = sums[2 * n], se = sums[2 * n + 1];
   const int64_t b = bias[n];
+  double c;
   if (mode == kModeF32) {
     r.beff = ms * (b - static_cast<int64_t>(act_zp) * sq) - static_cast<int64_t>(act_zp) * se;
-    r.c = ldexp(act_scale, es) / out_scale;
+    c = ldexp(act_scale, es) / out_scale;
     r.m_q = static_cast<int32_t>(ms);
     r.mul = 1u;
   } else {
     r.beff = b - static_cast<int64_t>(act_zp) * sq;
-    r.c = __dmul_rn(act_scale, static_cast<double>(s)) / out_scale;
+    c = __dmul_rn(act_scale, static_cast<double>(s)) / out_scale;
     r.m_q = 1;
     r.mul = static_cast<uint32_t>(ms);
   }
-  r.e2 = es + act_exp2;
+  // c = cm * 2^-cshift with cm the 53-bit integer mantissa (c is a normal double)
+  const uint64_t cb = static_cast<uint64_t>(__double_as_longlong(c));
+  const int cex = static_cast<int>((cb >> 52) & 0x7FF);
+  if (cex == 0 || cex == 0x7FF || 1075 - cex < 1 || 1075 - cex > 127) {
+    atomicCAS(bad_scale, 0, 2);  // requant multiplier outside the supported range
+  }
+  r.cm = (cb & ((1ull << 52) - 1)) | (1ull << 52);
+  r.cshift = static_cast<int16_t>(1075 - cex);
+  r.e2 = static_cast<int16_t>(es + act_exp2);
   rec[n] = r;
 }
 
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared, int* bad_scale,
                            cudaStream_t stream) {
   uint8_t* base = static_cast<uint8_t*>(prepared);
-  const size_t npad = static_cast<size_t>(plan->n_tiles) * plan->ch_per_tile;
   long long* sums = reinterpret_cast<long long*>(base + plan->plane_bytes + plan->record_bytes);
   cudaError_t e = cudaMemsetAsync(base, 0, plan->prepared_bytes, stream);
   if (e != cudaSuccess) return e;
@@ -500,7 +564,7 @@ cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* 
   p.K = plan->k;
   p.N = plan->n;
   p.k_pad = plan->k_pad;
-  p.ch_per_tile = plan->ch_per_tile;
+  p.b_rows = b_rows_for_mode(plan->mode);
   p.lpbq_block = plan->lpbq_block;
   p.weight = w->weight;
   p.lpbq = w->lpbq_block_scale;
@@ -508,7 +572,7 @@ cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* 
   p.sums = sums;
   const size_t total = static_cast<size_t>(plan->n) * (plan->k / 16);
   int blocks = static_cast<int>((total + 255) / 256);
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks > sm_count() * 32) blocks = sm_count() * 32;
   prepare_planes_kernel<<<blocks, 256, 0, stream>>>(p, w->weight_scale);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -516,7 +580,6 @@ cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* 
   prepare_records_kernel<<<static_cast<unsigned>((plan->n + 127) / 128), 128, 0, stream>>>(
       plan->mode, plan->n, w->weight_scale, w->bias_q, sums, plan->act_scale, plan->out_scale, plan->act_zp,
       plan->act_exp2, rec, bad_scale);
-  (void)npad;
   return cudaGetLastError();
 }
 
@@ -541,7 +604,7 @@ cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k,
                                int8_t* out, cudaStream_t stream) {
   const size_t total = static_cast<size_t>(n) * k;
   int blocks = static_cast<int>((total + 255) / 256);
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks > sm_count() * 32) blocks = sm_count() * 32;
   lpbq_expand_kernel<<<blocks, 256, 0, stream>>>(w4, bs, k, n, block, out);
   return cudaGetLastError();
 }

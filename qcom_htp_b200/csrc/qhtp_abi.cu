@@ -67,9 +67,11 @@ const char* qhtp_status_string(QhtpStatus status) {
 
 const char* qhtp_version(void) { return "qhtp-b200 0.1 (sm_100a)"; }
 
-int32_t qhtp_requant_code_host(int64_t T, double c, uint32_t mul, int32_t e2, uint64_t act_mant, uint64_t out_mant,
+int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2, uint64_t act_mant,
+                               uint64_t out_mant,
                                int32_t out_exp2, int32_t zp_out, int32_t qmax) {
-  return requant_code(T, c, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
+  if (cshift < 1 || cshift > 127) return -1;
+  return requant_code(T, cm, cshift, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
 }
 
 QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
@@ -112,7 +114,7 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
     p.ch_per_tile = 128;
   } else {
     p.mode = kModeExact;
-    p.ch_per_tile = 256;
+    p.ch_per_tile = 128;
   }
   p.n_tiles = (p.n + p.ch_per_tile - 1) / p.ch_per_tile;
   p.k_pad = static_cast<uint32_t>(align_up(p.k, kTileK));
@@ -120,7 +122,7 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   p.out_scale = w->out_scale;
   split_f64(w->act_scale, &p.act_mant, &p.act_exp2);
   split_f64(w->out_scale, &p.out_mant, &p.out_exp2);
-  p.plane_bytes = align_up(static_cast<size_t>(p.n_tiles) * kTileBRows * p.k_pad, 256);
+  p.plane_bytes = align_up(static_cast<size_t>(p.n_tiles) * b_rows_for_mode(p.mode) * p.k_pad, 256);
   const size_t npad = static_cast<size_t>(p.n_tiles) * p.ch_per_tile;
   p.record_bytes = align_up(npad * sizeof(ChannelRecord), 256);
   // planes | records | per-channel sums (prepare scratch) | 256-byte status word area

@@ -8,22 +8,23 @@
 // The output code is clip(round_half_even(z*), 0, qmax), the rounding of the reference oracle
 // (generate_qnn_matmul_python_cases.py:217 np.rint, :474-481).
 //
-// Fast path: z = double(T) * c + zp_out with c = double(mul*mA*2^e2/(mO*2^eO)); its absolute error
-// is below 6e-11 for |z| < 2^17.  Whenever z lies within kTieEps of a .5 boundary the decision is
-// redone exactly with 128-bit integer arithmetic.
+// Fast path, pure integer: with the float64 multiplier c = cm * 2^-s (cm its 53-bit mantissa),
+// T*cm is formed exactly in 128 bits and split into integer part and s-bit fraction.  c carries a
+// relative error <= 2^-52, i.e. <= 2^-35 absolute for |z - zp| < 2^17, so the rounding is decided
+// there unless the fraction lies within 2^-30 of one half; those elements are redone exactly with
+// 128-bit integer arithmetic on the unrounded scales.
 #pragma once
-#include <cmath>
 #include <cstdint>
 
 #ifdef __CUDACC__
 #define QHTP_HD __host__ __device__ __forceinline__
+#define QHTP_HD_NOINLINE static __host__ __device__ __noinline__
 #else
 #define QHTP_HD inline
+#define QHTP_HD_NOINLINE static
 #endif
 
 namespace qhtp {
-
-constexpr double kTieEps = 1e-9;
 
 struct U128 {
   uint64_t lo, hi;
@@ -61,6 +62,23 @@ QHTP_HD U128 shl128(U128 x, int s) {  // 0 <= s < 128
   return U128{x.lo << s, (x.hi << s) | (x.lo >> (64 - s))};
 }
 
+QHTP_HD U128 shr128(U128 x, int s) {  // 0 <= s < 128
+  if (s == 0) return x;
+  if (s >= 64) return U128{x.hi >> (s - 64), 0};
+  return U128{(x.lo >> s) | (x.hi << (64 - s)), x.hi >> s};
+}
+
+QHTP_HD U128 low_bits(U128 x, int s) {  // x mod 2^s, 1 <= s < 128
+  if (s >= 64) return U128{x.lo, s == 64 ? 0 : (x.hi & ((1ull << (s - 64)) - 1))};
+  return U128{x.lo & ((1ull << s) - 1), 0};
+}
+
+QHTP_HD U128 sub128(U128 a, U128 b) {  // a - b, a >= b
+  U128 r{a.lo - b.lo, a.hi - b.hi};
+  if (a.lo < b.lo) r.hi -= 1;
+  return r;
+}
+
 QHTP_HD int cmp128(U128 a, U128 b) {
   if (a.hi != b.hi) return a.hi < b.hi ? -1 : 1;
   if (a.lo != b.lo) return a.lo < b.lo ? -1 : 1;
@@ -75,16 +93,14 @@ QHTP_HD int cmp_scaled(U128 X, int ex, U128 Y, int ey) {
   const int lx = bx + d;  // bit length of X*2^d
   if (lx > by) return 1;
   if (lx < by) return -1;
-  // equal bit lengths (<= 128 on both sides): align exactly
-  if (d >= 0) return cmp128(shl128(X, d), Y);
+  if (d >= 0) return cmp128(shl128(X, d), Y);  // equal bit lengths (<= 128): align exactly
   return cmp128(X, shl128(Y, -d));
 }
 
-// Exact decision between floor(z) and floor(z)+1 for a z within 1e-9 of a .5 boundary.
+// Exact decision between r0 and r0 + 1, where r0 = floor(z*) for a z* within 1e-9 of r0 + 1/2.
 // |T| * mul must stay below 2^75 (so that |T|*mul*mA < 2^128): guaranteed by the K limit.
-QHTP_HD int64_t exact_round_near_tie(int64_t T, uint32_t mul, uint64_t mA, int e2, uint64_t mO, int eO,
-                                     int64_t zp_out, double z) {
-  const int64_t r0 = static_cast<int64_t>(floor(z));
+QHTP_HD_NOINLINE int64_t exact_round_near_tie(int64_t T, uint32_t mul, uint64_t mA, int e2, uint64_t mO, int eO,
+                                              int64_t zp_out, int64_t r0) {
   const int64_t hn = 2 * (r0 - zp_out) + 1;  // boundary = hn/2 (odd numerator, never 0)
   const uint64_t absT = T < 0 ? static_cast<uint64_t>(-(T + 1)) + 1u : static_cast<uint64_t>(T);
   const U128 L = mul_128x64(mul_64x64(absT, mul), mA);
@@ -105,28 +121,27 @@ QHTP_HD int64_t exact_round_near_tie(int64_t T, uint32_t mul, uint64_t mA, int e
   return (r0 % 2 == 0) ? r0 : r0 + 1;  // exact tie: half to even
 }
 
-#ifdef __CUDA_ARCH__
-__device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
-__device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
-__device__ __forceinline__ double i2d(int64_t v) { return __ll2double_rn(v); }
-#else
-inline double dmul(double a, double b) { return a * b; }
-inline double dadd(double a, double b) { return a + b; }
-inline double i2d(int64_t v) { return static_cast<double>(v); }
-#endif
-
-// Full requant of one element: returns the clipped output code.
-QHTP_HD int32_t requant_code(int64_t T, double c, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
+// Output code of one element.  cm/s: requant multiplier c = cm * 2^-s (1 <= s <= 127).
+QHTP_HD int32_t requant_code(int64_t T, uint64_t cm, int s, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
                              int32_t zp_out, int32_t qmax) {
-  const double z = dadd(dmul(i2d(T), c), static_cast<double>(zp_out));
-  if (!(z > -1.0)) return 0;                                       // also catches NaN
-  if (!(z < static_cast<double>(qmax) + 1.0)) return qmax;
+  const bool neg = T < 0;
+  const uint64_t a = neg ? static_cast<uint64_t>(-(T + 1)) + 1u : static_cast<uint64_t>(T);
+  const U128 P = mul_64x64(a, cm);  // |T| * cm, exact
+  const U128 ip = shr128(P, s);
+  if (ip.hi != 0 || ip.lo > (1ull << 20)) return neg ? 0 : qmax;  // |z - zp| > 2^20: far outside the range
+  const U128 f = low_bits(P, s);
+  const U128 half = shl128(U128{1, 0}, s - 1);
+  const int c = cmp128(f, half);
+  const U128 d = c >= 0 ? sub128(f, half) : sub128(half, f);
+  const int tol_bits = s - 30;  // tie window 2^-30, in units of 2^-s
+  const bool near = tol_bits > 0 ? (bitlen128(d) <= tol_bits) : (d.hi == 0 && d.lo <= 1);
   int64_t r;
-  const double f = z - floor(z);
-  if (fabs(f - 0.5) <= kTieEps) {
-    r = exact_round_near_tie(T, mul, mA, e2, mO, eO, zp_out, z);
+  if (near) {
+    const int64_t r0 = (neg ? -static_cast<int64_t>(ip.lo) - 1 : static_cast<int64_t>(ip.lo)) + zp_out;
+    r = exact_round_near_tie(T, mul, mA, e2, mO, eO, zp_out, r0);
   } else {
-    r = static_cast<int64_t>(rint(z));
+    const int64_t mag = static_cast<int64_t>(ip.lo) + (c > 0 ? 1 : 0);
+    r = (neg ? -mag : mag) + zp_out;
   }
   if (r < 0) r = 0;
   if (r > qmax) r = qmax;

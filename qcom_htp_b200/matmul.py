@@ -26,8 +26,8 @@ from . import _lib as L
 FAMILY_BITS = {"u8i8": (8, 8, 8), "w4a8": (8, 4, 8), "w8a16": (16, 8, 16), "w4a16": (16, 4, 16),
                "w16a16": (16, 16, 16)}
 
-RECORD_DTYPE = np.dtype([("beff", "<i8"), ("c", "<f8"), ("m_q", "<i4"), ("mul", "<u4"), ("e2", "<i4"),
-                         ("pad", "<i4")])
+RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cm", "<u8"), ("m_q", "<i4"), ("mul", "<u4"), ("e2", "<i2"),
+                         ("cshift", "<i2"), ("pad", "<i4")])
 
 
 def _stream_handle(stream) -> int:
@@ -211,7 +211,7 @@ def hmx_u16i16_to_u16_matmul(act, weight, weight_scale, bias_q, *, act_scale, ou
     return _one_shot("w16a16", act, weight, weight_scale, bias_q, act_scale, out_scale, **kw)
 
 
-def requant_code_host(T: int, c: float, mul: int, e2: int, act_mant: int, out_mant: int, out_exp2: int,
-                      zp_out: int, qmax: int) -> int:
+def requant_code_host(T: int, cm: int, cshift: int, mul: int, e2: int, act_mant: int, out_mant: int,
+                      out_exp2: int, zp_out: int, qmax: int) -> int:
     """The kernels' exact requant decision, evaluated on the host (testing aid)."""
-    return int(L.lib.qhtp_requant_code_host(T, c, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax))
+    return int(L.lib.qhtp_requant_code_host(T, cm, cshift, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax))

@@ -107,8 +107,9 @@ def test_requant_host_matches_rational_arithmetic(L):
         if abs(T) >= (1 << 62) or abs(T) * mul >= (1 << 75):
             continue   # outside the kernel's documented accumulator range
         c = float(Fraction(s_a) * Fraction(2) ** e_s / Fraction(s_o)) * mul
+        cm, ce = _split(c)
         want = min(max(round(T * exact_mult + zp), 0), qmax)
-        got = requant_code_host(T, c, mul, e_s + ea, ma, mo, eo, zp, qmax)
+        got = requant_code_host(T, cm, -ce, mul, e_s + ea, ma, mo, eo, zp, qmax)
         frac = T * exact_mult + zp
         if abs(frac - (frac.numerator // frac.denominator) - Fraction(1, 2)) < Fraction(1, 10 ** 9):
             n_tie += 1
@@ -118,9 +119,12 @@ def test_requant_host_matches_rational_arithmetic(L):
 
 def test_exact_tie_half_even(L):
     from qcom_htp_b200.matmul import requant_code_host
-    # act_scale = 1 (mant 2^52, exp -52), e_s = -1, out_scale = 1: value = T / 2
+    # act_scale = 1 (mant 2^52, exp -52), e_s = -1, out_scale = 1: value = T / 2; c = 0.5 = 2^52 * 2^-53
     # T=5 gives exactly 2.5 -> 2 ; T=7 -> 3.5 -> 4
-    assert requant_code_host(5, 0.5, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 2
-    assert requant_code_host(7, 0.5, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 4
-    assert requant_code_host(-1000, 0.5, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 0
-    assert requant_code_host(10 ** 6, 0.5, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 255
+    c = (1 << 52, 53)
+    assert requant_code_host(5, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 2
+    assert requant_code_host(7, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 4
+    assert requant_code_host(-1000, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 0
+    assert requant_code_host(10 ** 6, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 255
+    assert requant_code_host(-7, *c, 1, -53, 1 << 52, 1 << 52, -52, 128, 255) == 124   # 128 - 3.5 -> 124
+    assert requant_code_host(5, 1 << 52, 0, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == -1   # bad shift
