@@ -207,10 +207,13 @@ QhtpStatus qhtp_gdn_solve_u16(const uint16_t *A, int64_t n_chunks, int32_t C, in
 /* Library version string. */
 const char *qhtp_version(void);
 
+/* Text of the last CUDA error behind a QHTP_STATUS_RUNTIME_ERROR on the calling thread. */
+const char *qhtp_last_error_string(void);
+
 /* The exact requant decision the kernels use, on the host (for tests):
  * clip(round_half_even(T*mul*act_mant*2^e2 / (out_mant*2^out_exp2) + zp_out), 0, qmax), with the
- * same fixed-point fast path (multiplier c = cm * 2^-cshift, 1 <= cshift <= 127) and 128-bit exact
- * tie check as the device epilogue.  Returns -1 for a cshift outside [1, 127]. */
+ * same fixed-point fast path (multiplier c = cm * 2^-cshift, 31 <= cshift <= 127) and 128-bit exact
+ * tie check as the device epilogue.  Returns -1 for a cshift outside [31, 127]. */
 int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2,
                                uint64_t act_mant, uint64_t out_mant, int32_t out_exp2, int32_t zp_out,
                                int32_t qmax);

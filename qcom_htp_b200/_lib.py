@@ -65,6 +65,7 @@ class QhtpPreparedRun(C.Structure):
 SIGNATURES = {
     "qhtp_status_string": (C.c_char_p, [C.c_int]),
     "qhtp_version": (C.c_char_p, []),
+    "qhtp_last_error_string": (C.c_char_p, []),
     "qhtp_matmul_plan": (C.c_int, [C.POINTER(QhtpMatmulWeights), C.POINTER(QhtpMatmulPlan)]),
     "qhtp_matmul_prepared_bytes": (C.c_size_t, [C.POINTER(QhtpMatmulPlan)]),
     "qhtp_matmul_prepare": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.POINTER(QhtpMatmulWeights), C.c_void_p,
@@ -96,7 +97,10 @@ class QhtpError(RuntimeError):
 
     def __init__(self, fn: str, status: int):
         self.status = status
-        super().__init__(f"{fn} failed: {status_string(status)} ({status})")
+        detail = ""
+        if status == RUNTIME_ERROR:
+            detail = f": {lib.qhtp_last_error_string().decode()}"
+        super().__init__(f"{fn} failed: {status_string(status)} ({status}){detail}")
 
 
 def _load() -> C.CDLL:

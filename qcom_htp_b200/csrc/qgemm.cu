@@ -13,12 +13,16 @@
 //   * int16 weights (W16A16) are two byte planes, hi (s8) and lo (u8) (verify_w16a16_two_w8a16.py:21-48),
 //     giving three accumulators (hi*hi, hi*lo+lo*hi, lo*lo) combined with x65536 / x256 / x1.
 //
-// Persistent CTAs (one per SM) walk 128x128 output tiles.  Roles (320 threads):
+// Persistent CTAs (one per SM) walk 128x128 output tiles.  Roles (384 threads, 3 warpgroups):
 //   warp 0      TMA producer (one lane): activation plane(s) + weight planes per 128-byte K step
 //   warp 1      TMEM allocator + MMA issuer (one lane)
-//   warps 2..9  epilogue: each thread owns one output row and 64 channels; it drains the TMEM
+//   warps 2,3   idle (they complete warpgroup 0, which gives its registers to the epilogue)
+//   warps 4..11 epilogue: each thread owns one output row and 64 channels; it drains the TMEM
 //               accumulators into int64 registers, releases TMEM (the next tile's MMAs start),
 //               then requantizes from registers with integer fixed-point math and stores.
+// Register split: launched at 168 registers/thread (384 x 168 = 64512); warpgroup 0 drops to 40
+// (setmaxnreg.dec) and the two epilogue warpgroups rise to 232 (setmaxnreg.inc):
+// 128*40 + 256*232 = 64512, the launch total.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -91,7 +95,19 @@ struct GemmParams {
 };
 
 constexpr int kEpiWarps = 8;
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarp0 = 4;  // first epilogue warp (warpgroups 1 and 2)
+constexpr int kGemmThreads = 32 * (kEpiWarp0 + kEpiWarps);
+constexpr int kRegsLaunch = 168, kRegsCtrl = 40, kRegsEpi = 232;
+static_assert(kGemmThreads * kRegsLaunch == 128 * kRegsCtrl + 32 * kEpiWarps * kRegsEpi, "register split");
+
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 template <int PA, int MODE>
 struct GemmCfg {
@@ -122,8 +138,7 @@ __device__ __forceinline__ void load_record(const ChannelRecord* rec, ChannelRec
 }
 
 template <int PA, int MODE>
-// 320 threads x 200 registers = 64000 <= 65536: the epilogue keeps 64 int64 accumulators in registers.
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   using Cfg = GemmCfg<PA, MODE>;
   constexpr int S = Cfg::kStages;
@@ -160,6 +175,9 @@ __global__ void __maxnreg__(200)
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
+  if (warp < kEpiWarp0) {
+  // warpgroup 0: give registers to the epilogue warpgroups (setmaxnreg must dominate the code it governs)
+  regs_dec<kRegsCtrl>();
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -231,10 +249,12 @@ __global__ void __maxnreg__(200)
         if (ok) mma_commit(tfull);  // accumulators of this tile complete
       }
     }
+  }  // warps 2, 3: idle
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    regs_inc<kRegsEpi>();
+    // ------------------------------------------------------------------ epilogue (warps 4..11)
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;          // which 64 of the 128 channels
+    const int half = (warp - kEpiWarp0) >> 2;  // which 64 of the 128 channels
     const int row = quad * 32 + lane;
     const bool u16 = p.qmax > 255;
     uint32_t tc = 0;
@@ -297,12 +317,26 @@ __global__ void __maxnreg__(200)
           const int n = n0 + c0;
           if (n + 8 <= p.N) {  // channels past N (tile padding) have no record: skip them
             uint32_t code[8];
+            uint32_t near_mask = 0;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              ChannelRecord r;
-              load_record(rec + c0 + j, r);
-              code[j] = static_cast<uint32_t>(requant_code(T[c0 + j], r.cm, r.cshift, r.mul, r.e2, p.act_mant,
-                                                           p.out_mant, p.out_exp2, p.zp_out, p.qmax));
+              const uint4 rb = __ldg(reinterpret_cast<const uint4*>(rec + c0 + j));   // beff | cm
+              const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(rec + c0 + j) + 6);  // e2 | cshift
+              const uint64_t cm = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
+              bool nr;
+              code[j] = static_cast<uint32_t>(
+                  requant_fast(T[c0 + j], cm, static_cast<int>(sw >> 16), p.zp_out, p.qmax, &nr));
+              near_mask |= nr ? (1u << j) : 0u;
+            }
+            if (near_mask != 0) {  // rare: fraction within 2^-30 of a tie -> exact decision
+              for (int j = 0; j < 8; ++j) {
+                if (near_mask & (1u << j)) {
+                  ChannelRecord r;
+                  load_record(rec + c0 + j, r);
+                  code[j] = static_cast<uint32_t>(requant_code(T[c0 + j], r.cm, r.cshift, r.mul, r.e2, p.act_mant,
+                                                               p.out_mant, p.out_exp2, p.zp_out, p.qmax));
+                }
+              }
             }
             if (u16) {
               uint4 v;
@@ -542,7 +576,7 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
   // c = cm * 2^-cshift with cm the 53-bit integer mantissa (c is a normal double)
   const uint64_t cb = static_cast<uint64_t>(__double_as_longlong(c));
   const int cex = static_cast<int>((cb >> 52) & 0x7FF);
-  if (cex == 0 || cex == 0x7FF || 1075 - cex < 1 || 1075 - cex > 127) {
+  if (cex == 0 || cex == 0x7FF || 1075 - cex < 31 || 1075 - cex > 127) {
     atomicCAS(bad_scale, 0, 2);  // requant multiplier outside the supported range
   }
   r.cm = (cb & ((1ull << 52) - 1)) | (1ull << 52);

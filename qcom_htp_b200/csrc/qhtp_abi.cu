@@ -49,7 +49,13 @@ size_t a16_plane_bytes(const QhtpMatmulPlan* p, uint32_t m) {
 
 bool plan_ok(const QhtpMatmulPlan* p) { return p != nullptr && p->magic == kPlanMagic; }
 
-QhtpStatus from_cuda(cudaError_t e) { return e == cudaSuccess ? QHTP_STATUS_OK : QHTP_STATUS_RUNTIME_ERROR; }
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+QhtpStatus from_cuda(cudaError_t e) {
+  if (e == cudaSuccess) return QHTP_STATUS_OK;
+  g_last_cuda_error = e;
+  return QHTP_STATUS_RUNTIME_ERROR;
+}
 
 }  // namespace
 
@@ -67,10 +73,18 @@ const char* qhtp_status_string(QhtpStatus status) {
 
 const char* qhtp_version(void) { return "qhtp-b200 0.1 (sm_100a)"; }
 
+const char* qhtp_last_error_string(void) {
+  return g_last_cuda_error == cudaSuccess ? "no error" : cudaGetErrorString(g_last_cuda_error);
+}
+
 int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2, uint64_t act_mant,
                                uint64_t out_mant,
                                int32_t out_exp2, int32_t zp_out, int32_t qmax) {
-  if (cshift < 1 || cshift > 127) return -1;
+  if (cshift < 31 || cshift > 127) return -1;
+  // same sequence as the GEMM epilogue: branch-free fast path, exact decision near a tie
+  bool near = false;
+  const int32_t code = requant_fast(T, cm, cshift, zp_out, qmax, &near);
+  if (!near) return code;
   return requant_code(T, cm, cshift, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
 }
 

@@ -121,6 +121,49 @@ QHTP_HD_NOINLINE int64_t exact_round_near_tie(int64_t T, uint32_t mul, uint64_t 
   return (r0 % 2 == 0) ? r0 : r0 + 1;  // exact tie: half to even
 }
 
+// Branch-free fast path for the epilogue.  c = cm * 2^-s with 31 <= s <= 127 (checked at prepare).
+// Returns the clipped code computed as round_half_up(T*c) + zp, and sets *near when the fraction of
+// T*c lies within 2^-30 of one half (then the caller must use requant_code, which breaks the tie
+// exactly); away from ties round-half-up equals round-half-even.
+QHTP_HD int32_t requant_fast(int64_t T, uint64_t cm, int s, int32_t zp_out, int32_t qmax, bool* near) {
+  const bool neg = T < 0;
+  const uint64_t a = neg ? static_cast<uint64_t>(-(T + 1)) + 1u : static_cast<uint64_t>(T);
+  uint64_t lo = a * cm;
+#ifdef __CUDA_ARCH__
+  uint64_t hi = __umul64hi(a, cm);
+#else
+  uint64_t hi = static_cast<uint64_t>((static_cast<unsigned __int128>(a) * cm) >> 64);
+#endif
+  // |T*c| >= 2^20, i.e. P >> (s + 20) != 0, lies far outside [0, qmax] (zp < 2^16): saturate.
+  // Branches on s are uniform across a warp (one channel per step).
+  bool big;
+  if (s >= 108) {
+    big = false;  // P < 2^117 < 2^(s+20)
+  } else if (s >= 44) {
+    big = (hi >> (s - 44)) != 0;
+  } else {
+    big = hi != 0 || (lo >> (s + 20)) != 0;
+  }
+  // add one half at the binary point (bit s-1), then keep 30 fraction bits: W = (P + half) >> (s-30)
+  if (s - 1 >= 64) {
+    hi += 1ull << (s - 65);
+  } else {
+    const uint64_t lo2 = lo + (1ull << (s - 1));
+    hi += lo2 < lo ? 1ull : 0ull;
+    lo = lo2;
+  }
+  const int sh = s - 30;  // 1 <= sh <= 97
+  const uint64_t W = sh >= 64 ? (hi >> (sh - 64)) : ((lo >> sh) | (hi << (64 - sh)));
+  const uint32_t win = static_cast<uint32_t>(W) & 0x3FFFFFFFu;
+  *near = !big && ((win == 0u) | (win == 0x3FFFFFFFu));
+  const int64_t mag = static_cast<int64_t>(W >> 30);
+  int64_t r = (neg ? -mag : mag) + zp_out;
+  if (big) r = neg ? 0 : qmax;
+  r = r < 0 ? 0 : r;
+  r = r > qmax ? qmax : r;
+  return static_cast<int32_t>(r);
+}
+
 // Output code of one element.  cm/s: requant multiplier c = cm * 2^-s (1 <= s <= 127).
 QHTP_HD int32_t requant_code(int64_t T, uint64_t cm, int s, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
                              int32_t zp_out, int32_t qmax) {
