@@ -212,8 +212,8 @@ const char *qhtp_last_error_string(void);
 
 /* The exact requant decision the kernels use, on the host (for tests):
  * clip(round_half_even(T*mul*act_mant*2^e2 / (out_mant*2^out_exp2) + zp_out), 0, qmax), with the
- * same fixed-point fast path (multiplier c = cm * 2^-cshift, 31 <= cshift <= 127) and 128-bit exact
- * tie check as the device epilogue.  Returns -1 for a cshift outside [31, 127]. */
+ * same fixed-point fast path (multiplier c = cm * 2^-cshift, cshift >= 34, i.e. c < 2^18) and 128-bit exact
+ * tie check as the device epilogue.  Returns -1 for a cshift outside [34, 1074]. */
 int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2,
                                uint64_t act_mant, uint64_t out_mant, int32_t out_exp2, int32_t zp_out,
                                int32_t qmax);

@@ -409,8 +409,8 @@ def make_baseline_case(family: str, m: int, k: int, n: int, seed: int = 0x6D6D,
 # 3. Prepared record ("sidecar") and the exact requant model
 # ----------------------------------------------------------------------------------------------
 
-RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cm", "<u8"), ("m_q", "<i4"), ("mul", "<u4"),
-                         ("e2", "<i2"), ("cshift", "<i2"), ("pad", "<i4")])   # 32 bytes / output channel
+RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cmn", "<u8"), ("m_q", "<i4"), ("wbits", "<u4"),
+                         ("tn", "<i4"), ("pad", "<i4")])   # 32 bytes / output channel
 
 
 def split_f32(scale: np.ndarray):
@@ -449,18 +449,20 @@ def residual_plane(q: np.ndarray, m_s: np.ndarray) -> np.ndarray:
     return e.astype(np.int8)
 
 
-def prepare_record(case: QuantCase, dequant: str = "f32") -> tuple[np.ndarray, np.ndarray | None]:
+def prepare_record(case: QuantCase, dequant: str = "f32", return_c: bool = False):
     """Per-output-channel prepared record (the B200 "sidecar") and the e' plane.
 
     beff  : effective bias in T units.  f32 mode: m_s*(bias_q - zp*sum q) - zp*sum e';
             exact mode: bias_q - zp*sum q   (docs/qnn_custom_op_matmul_e2e.md:345-355 folds the
             activation zero-point into the bias the same way: bias_q - zp_act*sum_k w)
-    cm, cshift : the float64 requant multiplier c = cm * 2**-cshift (cm its 53-bit integer
-            mantissa), c = float64(s_A*2**e_s / s_O) in f32 mode, float64(float64(s_A*s_W)/s_O) in
-            exact mode; fast path z ~= T*c + zp_out evaluated exactly in fixed point (T*cm)
+    cmn, tn : the float64 requant multiplier c (float64(s_A*2**e_s / s_O) in f32 mode,
+            float64(float64(s_A*s_W)/s_O) in exact mode), written c = cm * 2**-cshift with cm its
+            53-bit integer mantissa, stored for the fixed-point fast path as (|T| << tn) * cmn *
+            2**-96: tn = 96 - cshift, cmn = cm; for c < 2**-44, tn = 0 and cmn = cm * 2**(96 -
+            cshift) rounded half up
     m_q   : multiplier of the q-plane accumulator inside T (m_s in f32 mode, 1 in exact mode)
-    mul   : extra integer factor of T in the exact tie check (1 in f32 mode, m_s in exact mode)
-    e2    : binary exponent so that  z* - zp_out = T*mul*mant(s_A)*2**e2 / s_O
+    wbits : the float32 weight scale's bits (its mantissa m_s and exponent e_s feed the exact tie
+            check: z* - zp_out = T*mul*mant(s_A)*2**(e_s + exp(s_A)) / s_O, mul = 1 or m_s)
     """
     fam = case.family
     if fam.schema == "per_group":
@@ -468,8 +470,6 @@ def prepare_record(case: QuantCase, dequant: str = "f32") -> tuple[np.ndarray, n
     wq = case.mma_weight.astype(np.int64)
     zp = fam.act_zp
     m_s, e_s = split_f32(case.weight_scale)
-    fa, ea = np.frexp(np.float64(case.act_scale))
-    ea_m = int(ea) - 53                                     # s_A = mant_A * 2**ea_m
     rec = np.zeros(wq.shape[0], RECORD_DTYPE)
     sum_q = wq.sum(axis=1)
     bias = case.bias_q.astype(np.int64)
@@ -479,25 +479,32 @@ def prepare_record(case: QuantCase, dequant: str = "f32") -> tuple[np.ndarray, n
         rec["beff"] = m_s * (bias - zp * sum_q) - zp * sum_e
         c = np.ldexp(np.float64(case.act_scale), e_s) / np.float64(case.out_scale)
         rec["m_q"] = m_s
-        rec["mul"] = 1
+        mul = np.ones_like(m_s)
     elif dequant == "exact":
         ep = None
         rec["beff"] = bias - zp * sum_q
         c = (np.float64(case.act_scale) * case.weight_scale.astype(np.float64)) / np.float64(case.out_scale)
         rec["m_q"] = 1
-        rec["mul"] = m_s
+        mul = m_s
     else:
         raise ValueError(dequant)
     fc, ec = np.frexp(c)
-    rec["cm"] = np.ldexp(fc, 53).astype(np.uint64)
-    rec["cshift"] = 53 - ec
-    rec["e2"] = e_s + ea_m
+    cm = np.ldexp(fc, 53).astype(np.uint64)
+    cshift = (53 - ec).astype(np.int64)
+    if np.any(cshift < 34):
+        raise ValueError("requant multiplier c >= 2**18 is outside the supported range")
+    small = cshift > 96
+    d = np.where(small, cshift - 96, 0)
+    cmn = cm.copy()
+    with np.errstate(over="ignore"):
+        rounded = (cm + (np.uint64(1) << np.maximum(d - 1, 0).astype(np.uint64))) >> d.astype(np.uint64)
+    cmn[small] = np.where(d[small] >= 64, 0, rounded[small])
+    rec["cmn"] = cmn
+    rec["tn"] = np.where(small, 0, 96 - cshift)
+    rec["wbits"] = np.asarray(case.weight_scale, np.float32).view(np.uint32)
+    if return_c:
+        return rec, ep, c, mul
     return rec, ep
-
-
-def record_c(rec: np.ndarray) -> np.ndarray:
-    """float64 requant multiplier c held by a record (exact: cm < 2**53)."""
-    return np.ldexp(rec["cm"].astype(np.float64), -rec["cshift"].astype(np.int64))
 
 
 def _exact_round(tpre: int, mul: int, e_s: int, s_a: float, s_o: float, zp_out: int) -> int:
@@ -513,7 +520,7 @@ TIE_EPS = 1e-9
 def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
     """Bit-exact output codes of the exact requant model (see module docstring)."""
     fam = case.family
-    rec, ep = prepare_record(case, dequant)
+    rec, ep, c, mul = prepare_record(case, dequant, return_c=True)
     xq = case.act_q.astype(np.float64)
     wq = case.mma_weight.astype(np.float64)
     # integer GEMMs in float64: every product and partial sum is an integer < 2**53 -> exact
@@ -521,14 +528,14 @@ def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
     tpre = rec["m_q"].astype(np.int64)[None, :] * p + rec["beff"][None, :]
     if ep is not None:
         tpre += (xq @ ep.astype(np.float64).T).astype(np.int64)
-    z = tpre.astype(np.float64) * record_c(rec)[None, :] + fam.out_zp
+    z = tpre.astype(np.float64) * c[None, :] + fam.out_zp
     r = np.rint(z)
     frac = z - np.floor(z)
     near = (np.abs(frac - 0.5) <= TIE_EPS) & (z > -1.0) & (z < fam.out_qmax + 1.0)
     if near.any():
         m_s, e_s = split_f32(case.weight_scale)
         for i, j in zip(*np.nonzero(near)):
-            r[i, j] = _exact_round(int(tpre[i, j]), int(rec["mul"][j]), int(e_s[j]),
+            r[i, j] = _exact_round(int(tpre[i, j]), int(mul[j]), int(e_s[j]),
                                    case.act_scale, case.out_scale, fam.out_zp)
     out = np.clip(r, 0, fam.out_qmax).astype(fam.out_dtype)
     if return_t:

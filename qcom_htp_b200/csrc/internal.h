@@ -26,11 +26,10 @@ inline constexpr uint32_t b_rows_for_mode(uint32_t mode) { return mode == kModeE
 
 struct ChannelRecord {  // 32 bytes, one per output channel (padded to the tile)
   int64_t beff;         // effective bias, in accumulator units
-  uint64_t cm;          // requant multiplier c = cm * 2^-cshift (cm: 53-bit mantissa of the float64 c)
+  uint64_t cmn;         // requant multiplier, applied as (|T| << tn) * cmn * 2^-96 (see fast_const)
   int32_t m_q;          // multiplier of the q-plane accumulator inside T
-  uint32_t mul;         // extra factor of T in the exact tie check
-  int16_t e2;           // binary exponent of the exact tie check
-  int16_t cshift;
+  uint32_t wbits;       // float32 weight-scale bits: mantissa/exponent for the exact tie check
+  int32_t tn;           // left shift of |T| in the fast path
   int32_t pad;
 };
 static_assert(sizeof(ChannelRecord) == 32, "record layout");

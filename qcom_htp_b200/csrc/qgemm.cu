@@ -90,7 +90,7 @@ struct GemmParams {
   void* out;
   int zp_out, qmax;
   uint64_t act_mant, out_mant;
-  int out_exp2;
+  int act_exp2, out_exp2;
   int* err;
 };
 
@@ -124,17 +124,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
-}
-
-__device__ __forceinline__ void load_record(const ChannelRecord* rec, ChannelRecord& r) {
-  const uint4* p = reinterpret_cast<const uint4*>(rec);
-  const uint4 a = __ldg(p), b = __ldg(p + 1);
-  r.beff = static_cast<int64_t>((static_cast<uint64_t>(a.y) << 32) | a.x);
-  r.cm = (static_cast<uint64_t>(a.w) << 32) | a.z;
-  r.m_q = static_cast<int32_t>(b.x);
-  r.mul = b.y;
-  r.e2 = static_cast<int16_t>(b.z & 0xFFFFu);
-  r.cshift = static_cast<int16_t>(b.z >> 16);
 }
 
 template <int PA, int MODE>
@@ -265,6 +254,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum)) break;
       tc_fence_after();
       const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+      // ---- drain: TMEM -> int64 accumulators in registers (64 channels of this thread's row)
       int64_t T[64];
 #pragma unroll
       for (int c0 = 0; c0 < 64; c0 += 8) {
@@ -311,48 +301,61 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);
-      if (m < p.M) {
+      // ---- requant + store, 16 channels per iteration; the register array rotates by 16 so the
+      // loop body is emitted once (small instruction footprint)
+      const bool row_ok = m < p.M;
+#pragma unroll 1
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        const int n = n0 + c0;
+        if (row_ok && n < p.N) {  // channels past N (tile padding) have no record
+          uint32_t code[16];
+          uint32_t near_mask = 0;
+          int64_t fl[16];
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 8) {
-          const int n = n0 + c0;
-          if (n + 8 <= p.N) {  // channels past N (tile padding) have no record: skip them
-            uint32_t code[8];
-            uint32_t near_mask = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const uint4 rb = __ldg(reinterpret_cast<const uint4*>(rec + c0 + j));   // beff | cm
-              const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(rec + c0 + j) + 6);  // e2 | cshift
-              const uint64_t cm = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
-              bool nr;
-              code[j] = static_cast<uint32_t>(
-                  requant_fast(T[c0 + j], cm, static_cast<int>(sw >> 16), p.zp_out, p.qmax, &nr));
-              near_mask |= nr ? (1u << j) : 0u;
-            }
-            if (near_mask != 0) {  // rare: fraction within 2^-30 of a tie -> exact decision
-              for (int j = 0; j < 8; ++j) {
-                if (near_mask & (1u << j)) {
-                  ChannelRecord r;
-                  load_record(rec + c0 + j, r);
-                  code[j] = static_cast<uint32_t>(requant_code(T[c0 + j], r.cm, r.cshift, r.mul, r.e2, p.act_mant,
-                                                               p.out_mant, p.out_exp2, p.zp_out, p.qmax));
-                }
+          for (int j = 0; j < 16; ++j) {
+            const uint4 rb = __ldg(reinterpret_cast<const uint4*>(rec + c0 + j));       // beff | cmn
+            const int tn = __ldg(reinterpret_cast<const int*>(rec + c0 + j) + 6);
+            const uint64_t cmn = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
+            bool nr;
+            code[j] = static_cast<uint32_t>(requant_fast96(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
+            near_mask |= nr ? (1u << j) : 0u;
+          }
+          if (near_mask != 0) {  // rare: within 2^-29 of a tie -> exact decision
+            for (int j = 0; j < 16; ++j) {
+              if (near_mask & (1u << j)) {
+                const uint32_t wb = __ldg(&rec[c0 + j].wbits);
+                const uint32_t ms = (wb & 0x7FFFFFu) | 0x800000u;
+                const int es = static_cast<int>((wb >> 23) & 0xFFu) - 150;
+                const uint32_t mul = MODE == kModeF32 ? 1u : ms;
+                code[j] = static_cast<uint32_t>(requant_tie(T[j], fl[j], mul, es + p.act_exp2, p.act_mant,
+                                                            p.out_mant, p.out_exp2, p.zp_out, p.qmax));
               }
             }
-            if (u16) {
-              uint4 v;
-              v.x = code[0] | (code[1] << 16);
-              v.y = code[2] | (code[3] << 16);
-              v.z = code[4] | (code[5] << 16);
-              v.w = code[6] | (code[7] << 16);
-              *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n) = v;
-            } else {
-              uint2 v;
-              v.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
-              v.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
-              *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n) = v;
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (n + 8 * h < p.N) {
+              const uint32_t* cd = code + 8 * h;
+              if (u16) {
+                uint4 v;
+                v.x = cd[0] | (cd[1] << 16);
+                v.y = cd[2] | (cd[3] << 16);
+                v.z = cd[4] | (cd[5] << 16);
+                v.w = cd[6] | (cd[7] << 16);
+                *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n +
+                                          8 * h) = v;
+              } else {
+                uint2 v;
+                v.x = cd[0] | (cd[1] << 8) | (cd[2] << 16) | (cd[3] << 24);
+                v.y = cd[4] | (cd[5] << 8) | (cd[6] << 16) | (cd[7] << 24);
+                *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n +
+                                          8 * h) = v;
+              }
             }
           }
         }
+#pragma unroll
+        for (int j = 0; j < 48; ++j) T[j] = T[j + 16];
       }
     }
   }
@@ -446,6 +449,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   prm.qmax = pl->out_qmax;
   prm.act_mant = pl->act_mant;
   prm.out_mant = pl->out_mant;
+  prm.act_exp2 = pl->act_exp2;
   prm.out_exp2 = pl->out_exp2;
   prm.err = g.err;
   switch (pl->mode * 2 + (pl->a_planes - 1)) {
@@ -546,14 +550,13 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
   const uint32_t ex = (bits >> 23) & 0xFFu;
   ChannelRecord r;
   r.pad = 0;
+  r.wbits = bits;
   if ((bits >> 31) != 0 || ex == 0 || ex == 0xFF) {  // negative, zero/subnormal, inf/nan
     atomicCAS(bad_scale, 0, 1);
     r.beff = 0;
-    r.cm = 0;
+    r.cmn = 0;
     r.m_q = 0;
-    r.mul = 0;
-    r.e2 = 0;
-    r.cshift = 0;
+    r.tn = 0;
     rec[n] = r;
     return;
   }
@@ -566,22 +569,22 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
     r.beff = ms * (b - static_cast<int64_t>(act_zp) * sq) - static_cast<int64_t>(act_zp) * se;
     c = ldexp(act_scale, es) / out_scale;
     r.m_q = static_cast<int32_t>(ms);
-    r.mul = 1u;
   } else {
     r.beff = b - static_cast<int64_t>(act_zp) * sq;
     c = __dmul_rn(act_scale, static_cast<double>(s)) / out_scale;
     r.m_q = 1;
-    r.mul = static_cast<uint32_t>(ms);
   }
   // c = cm * 2^-cshift with cm the 53-bit integer mantissa (c is a normal double)
   const uint64_t cb = static_cast<uint64_t>(__double_as_longlong(c));
   const int cex = static_cast<int>((cb >> 52) & 0x7FF);
-  if (cex == 0 || cex == 0x7FF || 1075 - cex < 31 || 1075 - cex > 127) {
-    atomicCAS(bad_scale, 0, 2);  // requant multiplier outside the supported range
+  const int cshift = 1075 - cex;
+  if (cex == 0 || cex == 0x7FF || cshift < 34) {
+    atomicCAS(bad_scale, 0, 2);  // requant multiplier outside the supported range (c >= 2^18)
   }
-  r.cm = (cb & ((1ull << 52) - 1)) | (1ull << 52);
-  r.cshift = static_cast<int16_t>(1075 - cex);
-  r.e2 = static_cast<int16_t>(es + act_exp2);
+  const FastConst fc = fast_const((cb & ((1ull << 52) - 1)) | (1ull << 52), cshift);
+  r.cmn = fc.cmn;
+  r.tn = fc.tn;
+  (void)act_exp2;
   rec[n] = r;
 }
 

@@ -80,12 +80,15 @@ const char* qhtp_last_error_string(void) {
 int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2, uint64_t act_mant,
                                uint64_t out_mant,
                                int32_t out_exp2, int32_t zp_out, int32_t qmax) {
-  if (cshift < 31 || cshift > 127) return -1;
-  // same sequence as the GEMM epilogue: branch-free fast path, exact decision near a tie
+  if (cshift < 34 || cshift > 1074) return -1;
+  // same sequence as the GEMM epilogue: per-channel fast constants, branch-free fast path, exact
+  // decision near a tie
+  const FastConst fc = fast_const(cm, cshift);
   bool near = false;
-  const int32_t code = requant_fast(T, cm, cshift, zp_out, qmax, &near);
+  int64_t fl = 0;
+  const int32_t code = requant_fast96(T, fc.cmn, fc.tn, zp_out, qmax, &near, &fl);
   if (!near) return code;
-  return requant_code(T, cm, cshift, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
+  return requant_tie(T, fl, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
 }
 
 QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {

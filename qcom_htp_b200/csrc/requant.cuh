@@ -164,6 +164,63 @@ QHTP_HD int32_t requant_fast(int64_t T, uint64_t cm, int s, int32_t zp_out, int3
   return static_cast<int32_t>(r);
 }
 
+// Per-channel constants of the epilogue fast path: the float64 multiplier c = cm * 2^-cshift
+// (cm its 53-bit mantissa) is applied as  V = (|T| << tn) * cmn * 2^-96, i.e. tn = 96 - cshift and
+// cmn = cm, so the binary point of the 128-bit product sits at bit 96 for every channel.  Channels
+// with c < 2^-44 (cshift > 96) use tn = 0 and cmn = cm * 2^(96-cshift) rounded half up.
+// Requires c < 2^18 (cshift >= 34).
+struct FastConst {
+  uint64_t cmn;
+  int tn;
+};
+
+QHTP_HD FastConst fast_const(uint64_t cm, int cshift) {
+  if (cshift <= 96) return FastConst{cm, 96 - cshift};
+  const int d = cshift - 96;
+  if (d >= 64) return FastConst{0, 0};
+  return FastConst{(cm + (1ull << (d - 1))) >> d, 0};
+}
+
+// Branch-free fast path.  Returns clip(round_half_up(T*c) + zp) and sets *near when the result may
+// differ from round-half-even of the exact value: the 30 fraction bits below the binary point are
+// within 2 units (2^-29) of a tie.  Error budget of V: truncation of the low product bits < 2^-30,
+// cmn rounding <= 2^-34, c itself (a float64) <= 2^-33 for |V| < 2^19.  |T| >= 2^(63-tn) means
+// |V| >= 2^19, which saturates.
+QHTP_HD int32_t requant_fast96(int64_t T, uint64_t cmn, int tn, int32_t zp_out, int32_t qmax, bool* near,
+                               int64_t* floor_v) {
+  const bool neg = T < 0;
+  const uint64_t a = neg ? static_cast<uint64_t>(-(T + 1)) + 1u : static_cast<uint64_t>(T);
+  const bool big = (a >> (63 - tn)) != 0;
+  const uint64_t ap = a << tn;  // < 2^63 unless big
+#ifdef __CUDA_ARCH__
+  const uint64_t hi = __umul64hi(ap, cmn);
+#else
+  const uint64_t hi = static_cast<uint64_t>((static_cast<unsigned __int128>(ap) * cmn) >> 64);
+#endif
+  // W = floor((P + 2^95) / 2^66): rounded magnitude above 30 fraction bits
+  const uint64_t W = (hi + (1ull << 31)) >> 2;
+  const uint32_t win = static_cast<uint32_t>(W) & 0x3FFFFFFFu;
+  *near = !big && (((win + 2u) & 0x3FFFFFFFu) < 4u);
+  const int64_t mag = static_cast<int64_t>(W >> 30);
+  // floor of the signed value (meaningful when *near): |V| + 1/2 sits next to an integer boundary
+  const int64_t fl_mag = win < (1u << 29) ? mag - 1 : mag;  // floor(|V|)
+  *floor_v = (neg ? -fl_mag - 1 : fl_mag) + zp_out;
+  int64_t r = (neg ? -mag : mag) + zp_out;
+  if (big) r = neg ? 0 : qmax;
+  r = r < 0 ? 0 : r;
+  r = r > qmax ? qmax : r;
+  return static_cast<int32_t>(r);
+}
+
+// Exact code for an element flagged by requant_fast96; floor_v = floor(z*) from the fast path.
+QHTP_HD int32_t requant_tie(int64_t T, int64_t floor_v, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
+                            int32_t zp_out, int32_t qmax) {
+  int64_t r = exact_round_near_tie(T, mul, mA, e2, mO, eO, zp_out, floor_v);
+  r = r < 0 ? 0 : r;
+  r = r > qmax ? qmax : r;
+  return static_cast<int32_t>(r);
+}
+
 // Output code of one element.  cm/s: requant multiplier c = cm * 2^-s (1 <= s <= 127).
 QHTP_HD int32_t requant_code(int64_t T, uint64_t cm, int s, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
                              int32_t zp_out, int32_t qmax) {

@@ -26,8 +26,8 @@ from . import _lib as L
 FAMILY_BITS = {"u8i8": (8, 8, 8), "w4a8": (8, 4, 8), "w8a16": (16, 8, 16), "w4a16": (16, 4, 16),
                "w16a16": (16, 16, 16)}
 
-RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cm", "<u8"), ("m_q", "<i4"), ("mul", "<u4"), ("e2", "<i2"),
-                         ("cshift", "<i2"), ("pad", "<i4")])
+RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cmn", "<u8"), ("m_q", "<i4"), ("wbits", "<u4"), ("tn", "<i4"),
+                         ("pad", "<i4")])
 
 
 def _stream_handle(stream) -> int:

@@ -127,4 +127,4 @@ def test_exact_tie_half_even(L):
     assert requant_code_host(-1000, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 0
     assert requant_code_host(10 ** 6, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 255
     assert requant_code_host(-7, *c, 1, -53, 1 << 52, 1 << 52, -52, 128, 255) == 124   # 128 - 3.5 -> 124
-    assert requant_code_host(5, 1 << 52, 30, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == -1   # bad shift
+    assert requant_code_host(5, 1 << 52, 33, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == -1   # bad shift
