@@ -141,6 +141,22 @@ size_t qhtp_matmul_workspace_bytes(const QhtpMatmulPlan *plan, uint32_t m);
 QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* qhtp_matmul_run without a caller workspace.  No counterpart in the reference.
+ * For callers that may not allocate device memory when they run the op -- e.g. an inference-runtime
+ * plugin called from the runtime's execute step, where the runtime owns and pre-plans every device
+ * buffer, or a latency-critical thread that cannot afford an allocation's implicit synchronization.
+ * The u16 activation planes and the error word live in a fixed area inside the library
+ * (QHTP_NOALLOC_SCRATCH_BYTES of device memory, held by every GPU that loads the library until the
+ * process exits), so M*K is limited: the call needs qhtp_matmul_workspace_bytes(plan, m) <=
+ * QHTP_NOALLOC_SCRATCH_BYTES (for u16 activations 2*M*K + 256 bytes; u8 activations need only 256)
+ * and returns QHTP_STATUS_INVALID_ARGUMENT with a qhtp_last_error_string message otherwise.  The
+ * first call on each device looks up the area's device address: make it before any stream capture.
+ * All calls share the area: calls whose work overlaps on the GPU race, so serialize them.  Calls no
+ * cudaMalloc / cudaFree.  Device-side pipeline timeouts are not reported by this entry point. */
+#define QHTP_NOALLOC_SCRATCH_BYTES (8u << 20)
+QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
+                                   void *stream);
+
 /* Synchronize `stream` and read the device error word of `workspace`; clears it.  Returns
  * QHTP_STATUS_RUNTIME_ERROR if a kernel recorded an error (code in *device_code if non-NULL). */
 QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan *plan, void *workspace, uint32_t m, int *device_code,

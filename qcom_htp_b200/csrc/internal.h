@@ -44,6 +44,11 @@ struct GemmLaunch {
   cudaStream_t stream;
 };
 
+// qhtp_abi.cu: status of a CUDA result (records the error for qhtp_last_error_string), and a
+// validation message for qhtp_last_error_string (static storage only)
+QhtpStatus status_from_cuda(cudaError_t e);
+void set_last_message(const char* msg);
+
 // qgemm.cu
 cudaError_t launch_gemm(const GemmLaunch& g);
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,

@@ -49,14 +49,27 @@ size_t a16_plane_bytes(const QhtpMatmulPlan* p, uint32_t m) {
 
 bool plan_ok(const QhtpMatmulPlan* p) { return p != nullptr && p->magic == kPlanMagic; }
 
-thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+}  // namespace
 
-QhtpStatus from_cuda(cudaError_t e) {
+namespace qhtp {
+
+// Last failure on the calling thread: a CUDA error, or a message from host-side validation.
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+thread_local const char* g_last_message = nullptr;
+
+QhtpStatus status_from_cuda(cudaError_t e) {
   if (e == cudaSuccess) return QHTP_STATUS_OK;
   g_last_cuda_error = e;
+  g_last_message = nullptr;
   return QHTP_STATUS_RUNTIME_ERROR;
 }
 
+void set_last_message(const char* msg) { g_last_message = msg; }
+
+}  // namespace qhtp
+
+namespace {
+QhtpStatus from_cuda(cudaError_t e) { return qhtp::status_from_cuda(e); }
 }  // namespace
 
 extern "C" {
@@ -74,7 +87,8 @@ const char* qhtp_status_string(QhtpStatus status) {
 const char* qhtp_version(void) { return "qhtp-b200 0.1 (sm_100a)"; }
 
 const char* qhtp_last_error_string(void) {
-  return g_last_cuda_error == cudaSuccess ? "no error" : cudaGetErrorString(g_last_cuda_error);
+  if (qhtp::g_last_message != nullptr) return qhtp::g_last_message;
+  return qhtp::g_last_cuda_error == cudaSuccess ? "no error" : cudaGetErrorString(qhtp::g_last_cuda_error);
 }
 
 int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t mul, int32_t e2, uint64_t act_mant,
