@@ -19,7 +19,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -31,6 +30,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from one
+# `ncu --set full` capture of this script's own workload (bench.py --steps 1 --warmup 3 ...)
+NCU_TRAFFIC_BYTES = {
+    ("qgemm", 4096, 4096, 14336): 153_884_160 + 100_395_264,
+    ("gdn", 4096): 337_263_104 + 1_020_883_000,
+}
 
 
 def peaks() -> dict:
@@ -93,47 +99,68 @@ def synth_gdn_A(n_chunks: int, C: int, dk: int, seed: int, device) -> torch.Tens
 # clocks
 # ----------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, max clock and clock-event reasons through NVML (read-only) every ~2 ms in a
+    background thread; summary() reports the samples taken inside the marked timed window."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []          # (t, sm_mhz, max_mhz, reason_bits)
+        self.window = None
+        self.err = None
+
+    def _handle(self, nv):
+        try:
+            props = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.bits = {name: getattr(nv, attr) for name, attr in self.REASONS}
+            while not self._stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((time.perf_counter(), sm, rs))
+                self._stop.wait(0.002)
+        except Exception as e:  # NVML missing or not permitted: report it
+            self.err = repr(e)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        import threading
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        time.sleep(0.01)
         return self
 
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
+
     def __exit__(self, *a):
-        self.samples = []
-        if self.proc is None:
-            return
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        for line in out.strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 7:
-                self.samples.append(parts)
+        self._stop.set()
+        self._t.join(timeout=5)
 
     def summary(self) -> dict:
-        if not getattr(self, "samples", None):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(p[0]) for p in self.samples if p[0].replace(".", "").isdigit()]
-        mx = [float(p[1]) for p in self.samples if p[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for p in self.samples for i in range(4) if p[3 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        if self.err or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"nvml unavailable: {self.err}"]}
+        sel = self.samples
+        if self.window:
+            inside = [x for x in self.samples if self.window[0] <= x[0] <= self.window[1]]
+            sel = inside or sel
+        reasons = sorted({n for _, _, rs in sel for n, b in self.bits.items() if rs & b})
+        return {"sm_mhz": statistics.median(x[1] for x in sel), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sel), "source": "NVML, 2 ms, timed window"}
 
 
 # ----------------------------------------------------------------------------------------------
@@ -169,12 +196,13 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
-def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, stream) -> list[float]:
+def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, stream, clk=None) -> list[float]:
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    t_host0 = time.perf_counter()
     times = []
     for _ in range(steps):
         flush.add_(1)                      # evict L2 (256 MB write) outside the timed window
@@ -186,6 +214,8 @@ def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, st
         e1.synchronize()
         times.append(e0.elapsed_time(e1) * 1e-3)
     torch.cuda.synchronize()
+    if clk is not None:
+        clk.mark(t_host0, time.perf_counter())
     barrier(world)
     return times
 
@@ -275,7 +305,7 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     fn = lambda: op(act, out)
     with ClockSampler(local) as clk:
-        times = timed_steps(fn, args.steps, args.warmup, flush, world, stream)
+        times = timed_steps(fn, args.steps, args.warmup, flush, world, stream, clk)
     op.check_device(m)
     t_step = max_over_ranks(statistics.mean(times), world)
     ops = 2.0 * m * n * k
@@ -308,7 +338,8 @@ def run_gemm(args, world, rank, local, stream) -> dict:
         "e2e": {"value": ops * world / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
                 "d2h_bytes_per_step": m * n * 2},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                     "frac": achieved / int8_peak, "traffic": None, "op_kind": "int8 MAC x2, logical",
+                     "frac": achieved / int8_peak, "op_kind": "int8 MAC x2, logical",
+                     "traffic": NCU_TRAFFIC_BYTES.get(("qgemm", m, k, n)),
                      "executed_tflops": executed, "frac_executed": executed / int8_peak,
                      "peak_src": f"2 x bf16_tflops ({pk['src']}, burst)",
                      "kernel": "split_u16_planes + qgemm_kernel<2,F32> (one qhtp_matmul_run)"},
@@ -341,7 +372,7 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
     fn = lambda: gdn_inverse(A, T)
     steps = args.steps
     with ClockSampler(local) as clk:
-        times = timed_steps(fn, steps, args.warmup, flush, world, stream)
+        times = timed_steps(fn, steps, args.warmup, flush, world, stream, clk)
     t = max_over_ranks(statistics.mean(times), world)
     pk = peaks()
     bytes_alg = n_chunks * (C * C * 2 + C * C * 4)       # read A (bf16), write T (fp32)
@@ -350,7 +381,7 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
            "ms_per_step": t * 1e3, "config": {"workload": "GDN C=256 inverse", "chunks_per_gpu": n_chunks,
                                              "note": "batch 8 x 32 heads x 16 chunks per GPU"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                        "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                        "frac": achieved / pk["hbm_gbs"], "traffic": NCU_TRAFFIC_BYTES.get(("gdn", n_chunks)),
                         "peak_src": f"hbm_gbs ({pk['src']})"},
            "gpu_launches": steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
