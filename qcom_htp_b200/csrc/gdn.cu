@@ -467,6 +467,7 @@ cudaError_t launch_any(const GdnIO& io, int C, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_gdn_bf16(const void* A, float* T, int64_t n_chunks, int C, cudaStream_t stream) {
+  if (C == 256 && gdn256_supported(A, T, n_chunks)) return launch_gdn256_bf16(A, T, n_chunks, stream);
   GdnIO io{A, T, n_chunks, 0, 0, 1.0f, 1.0f, nullptr};
   return launch_any<false>(io, C, stream);
 }

@@ -140,11 +140,13 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, int a_signed, int 
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
-// Instruction descriptor, kind::f16 with bf16 inputs and f32 accumulate, both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+// Instruction descriptor, kind::f16 with bf16 inputs and f32 accumulate; A K-major, B K-major
+// (b_mn_major = 0) or MN-major (b_mn_major = 1, bit 16).
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major = 0) {
   return (1u << 4)             // D format: F32
          | (1u << 7)           // A: BF16
          | (1u << 10)          // B: BF16
+         | (static_cast<uint32_t>(b_mn_major) << 16)
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
@@ -184,5 +186,53 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 bit x 32 columns: thread i of the warp receives TMEM lane (base_lane + i),
+// columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor for an MN-major operand stored with the 128-byte swizzle: each
+// 128-byte row holds 64 consecutive MN elements of one K index, 8-row swizzle atoms are 1024 bytes
+// apart along K (SBO), and consecutive 64-element MN groups are `lbo_bytes` apart (LBO).  Byte for
+// byte this is the image of a row-major [K][64] bf16 tile written with the 128-byte swizzle, so one
+// row-major image serves as a K-major A operand and as an MN-major B operand.  A K step of 16 is
+// +2048 bytes of start address.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;  // LBO: MN-group stride
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                    // SBO: 8-row K-group stride
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// ------------------------------------------------------------------------------------------------
+// TMA stores (shared -> global, bulk async-group completion)
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of every committed bulk store of this thread have been read.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 }  // namespace qhtp
