@@ -51,6 +51,11 @@ void set_last_message(const char* msg);
 
 // qgemm.cu
 cudaError_t launch_gemm(const GemmLaunch& g);
+// qdecode.cu: channel-major (swap-AB) kernel for M <= kDecodeMaxM activation rows; a_base is the
+// u8 activation or the [hi; lo] byte planes of a u16 activation
+constexpr uint32_t kDecodeMaxM = 64;
+bool decode_supported(const QhtpMatmulPlan* plan, uint32_t m);
+cudaError_t launch_decode(const GemmLaunch& g, const uint8_t* a_base);
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
                            int* bad_scale, cudaStream_t stream);
 cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k, uint32_t n, uint32_t block,
@@ -64,9 +69,12 @@ cudaError_t launch_gdn_u16(const uint16_t* A, int64_t n_chunks, int C, int zpA, 
 bool gdn256_supported(const void* A, const void* T, int64_t n_chunks);
 cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaStream_t stream);
 
-// tensor maps (qgemm.cu); all use the 128-byte swizzle
+// tensor maps (qgemm.cu)
 bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t rows,
-                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+// prepared weight planes: box (tile, K block) at row (tile * kblocks + kb) * b_rows, copied verbatim
+bool make_tmap_planes(CUtensorMap* map, const QhtpMatmulPlan* plan);
 bool make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
                      uint32_t box_inner, uint32_t box_rows);
 

@@ -1,0 +1,418 @@
+// Decode-shaped quantized GEMM (few activation rows, M <= 64) on B200.
+//
+// Same operation and exactness model as qgemm.cu (HmxU16I4ToU16MatMul and the rest of the QNN
+// MatMul family, requant as generate_qnn_matmul_python_cases.py:426-525), with the roles of the
+// operands swapped for small M:
+//   D[ch, tok] = sum_k W[ch, k] * X[tok, k]
+// The 128 output channels of a weight tile are the MMA's M = 128 (one TMEM lane per channel) and
+// the M activation rows are its N (16, 32 or 64 columns), so the tensor work per weight byte is
+// N/128 of the row-tiled kernel's and the kernel is bound by streaming the prepared weight planes.
+// The prepared planes are used as they are: for each 128-channel tile, rows [q | e'] (f32 weight
+// dequant), [q] (exact dequant) or [hi | lo] (int16 weights), K contiguous, which is the K-major
+// A operand; the activation (u8, or the hi/lo byte planes of u16) is the K-major B operand.
+//
+// Weight tiles alone (N/128 of them) cannot fill 148 SMs for N = 4096, so K is split over the CTAs
+// of a thread-block cluster.  Each CTA accumulates its K range in TMEM and parks its int32 partial
+// accumulators in its own shared memory; then each CTA sums one slice of the activation rows over
+// the whole cluster through distributed shared memory and requantizes that slice.  The int32 plane sums are exact for the
+// supported K (<= 32768), so the split changes no output bit.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps 2..5
+// epilogue (TMEM lane quadrants 2, 3, 0, 1).  Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+#include "requant.cuh"
+
+namespace qhtp {
+
+namespace {
+
+constexpr int kDecThreads = 192;
+constexpr int kDecEpiWarp0 = 2;
+
+struct DecodeParams {
+  int M, N, kblocks, splits;
+  const ChannelRecord* rec;
+  void* out;
+  int zp_out, qmax;
+  uint64_t act_mant, out_mant;
+  int act_exp2, out_exp2;
+  int* err;
+};
+
+// Accumulators per mode and activation-plane count (TMEM column groups of MP columns each).
+template <int MODE, int PA>
+struct DecAcc {
+  static constexpr int kWPlanes = MODE == kModeExact ? 1 : 2;  // weight planes per tile
+  static constexpr int kAcc = MODE == kModeW16 ? 3 : kWPlanes * PA;
+};
+
+template <int MODE, int PA, int MP>
+struct DecCfg {
+  static constexpr int kAcc = DecAcc<MODE, PA>::kAcc;
+  static constexpr int kWRows = 128 * DecAcc<MODE, PA>::kWPlanes;
+  static constexpr int kStageW = kWRows * kTileK;    // weight planes of one 128-deep K block
+  static constexpr int kStageX = MP * kTileK;        // one activation plane
+  static constexpr int kStage = kStageW + PA * kStageX;
+  static constexpr int kStages = (192 * 1024) / kStage > 8 ? 8 : (192 * 1024) / kStage;
+  static constexpr int kRedBytes = kAcc * MP * 128 * 4;  // int32 partials of one CTA
+  static constexpr int kPipeBytes = kStages * kStage;
+  static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024 + 256;
+  static constexpr uint32_t kTmemCols = kAcc * MP <= 32 ? 32 : (kAcc * MP <= 64 ? 64 : (kAcc * MP <= 128 ? 128 : 256));
+  static_assert(kAcc * MP <= 256, "accumulators exceed the TMEM allocation");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Plain (non-volatile) load from distributed shared memory: ordering against the partial-sum stores
+// comes from the cluster barrier, so independent loads may be scheduled together.
+__device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
+  int32_t v;
+  asm("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+template <int MODE, int PA, int MP>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    qdecode_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                   const DecodeParams p) {
+  using Cfg = DecCfg<MODE, PA, MP>;
+  constexpr int S = Cfg::kStages;
+  constexpr int NA = Cfg::kAcc;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int red_region = Cfg::kPipeBytes > Cfg::kRedBytes ? Cfg::kPipeBytes : Cfg::kRedBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + red_region);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+  int32_t* red = reinterpret_cast<int32_t*>(smem);  // [acc][tok][ch] partials (after the K loop)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int splits = p.splits;
+  const uint32_t crank = splits > 1 ? cluster_rank() : 0u;
+  const int tile = blockIdx.x / splits;
+  const int kb0 = static_cast<int>((static_cast<int64_t>(p.kblocks) * crank) / splits);
+  const int kb1 = static_cast<int>((static_cast<int64_t>(p.kblocks) * (crank + 1)) / splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  bool ok = true;
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW);
+      int i = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+        uint8_t* st = smem + s * Cfg::kStage;
+        tma_load_2d(st, &tmW, &full[s], 0, (tile * p.kblocks + kb) * Cfg::kWRows);
+#pragma unroll
+        for (int pl = 0; pl < PA; ++pl)
+          tma_load_2d(st + Cfg::kStageW + pl * Cfg::kStageX, &tmX, &full[s], kb * kTileK, pl * p.M);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int i = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&full[s], (i / S) & 1, p.err, kErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * Cfg::kStage);
+        const uint64_t dW0 = desc_kmajor_sw128(st);
+        const uint64_t dW1 = desc_kmajor_sw128(st + 128 * kTileK);
+        const uint64_t dX0 = desc_kmajor_sw128(st + Cfg::kStageW);
+        const uint64_t dX1 = desc_kmajor_sw128(st + Cfg::kStageW + (PA > 1 ? Cfg::kStageX : 0));
+#pragma unroll
+        for (int kk = 0; kk < kTileK / 32; ++kk) {
+          const uint32_t acc = (i | kk) ? 1u : 0u;
+          const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
+          if constexpr (MODE == kModeW16) {
+            constexpr uint32_t idS = idesc_i8(128, MP, 1, 0);  // s8 hi-byte weight x u8 act
+            constexpr uint32_t idU = idesc_i8(128, MP, 0, 0);  // u8 lo-byte weight x u8 act
+            mma_i8(tmem + 0 * MP, dW0 + ko, dX0 + ko, idS, acc);   // hi x hi
+            mma_i8(tmem + 1 * MP, dW0 + ko, dX1 + ko, idS, acc);   // hi x lo
+            mma_i8(tmem + 1 * MP, dW1 + ko, dX0 + ko, idU, 1u);    // + lo x hi
+            mma_i8(tmem + 2 * MP, dW1 + ko, dX1 + ko, idU, acc);   // lo x lo
+          } else {
+            constexpr uint32_t id = idesc_i8(128, MP, 1, 0);       // s8 weight x u8 act
+            mma_i8(tmem + 0 * MP, dW0 + ko, dX0 + ko, id, acc);                     // q x x(_hi)
+            if constexpr (MODE == kModeF32) mma_i8(tmem + 1 * MP, dW1 + ko, dX0 + ko, id, acc);  // e' x x(_hi)
+            if constexpr (PA == 2) {
+              constexpr int lo = MODE == kModeF32 ? 2 : 1;
+              mma_i8(tmem + lo * MP, dW0 + ko, dX1 + ko, id, acc);                  // q x x_lo
+              if constexpr (MODE == kModeF32) mma_i8(tmem + 3 * MP, dW1 + ko, dX1 + ko, id, acc);
+            }
+          }
+        }
+        mma_commit(&empty[s]);
+      }
+      if (ok) mma_commit(tfull);
+    }
+  }
+
+  // All MMAs of this CTA complete (or it gave up) before the pipeline buffers turn into the
+  // partial-sum area.
+  const bool is_epi = warp >= kDecEpiWarp0;
+  const int quad = warp & 3;
+  const int ch_local = quad * 32 + lane;                       // TMEM lane = channel in the tile
+  const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  if (is_epi) {
+    ok = mbar_wait(tfull, 0, p.err, kErrTimeoutAccum);
+    tc_fence_after();
+  }
+  __syncthreads();
+
+  // Per-channel requant constants (one channel per epilogue thread).
+  const int n = tile * 128 + ch_local;
+  const bool ch_ok = is_epi && n < p.N;
+  int64_t beff = 0, mq = 0;
+  uint64_t cmn = 0;
+  int tn = 0, es = 0;
+  uint32_t mul = 1;
+  if (ch_ok) {
+    const ChannelRecord* rc = p.rec + n;
+    beff = rc->beff;
+    cmn = rc->cmn;
+    tn = rc->tn;
+    mq = rc->m_q;
+    const uint32_t wb = rc->wbits;
+    es = static_cast<int>((wb >> 23) & 0xFFu) - 150;
+    mul = MODE == kModeF32 ? 1u : ((wb & 0x7FFFFFu) | 0x800000u);
+  }
+  const bool u16 = p.qmax > 255;
+  auto emit = [&](int tok, const int32_t (&a)[NA]) {
+    int64_t T;
+    if constexpr (MODE == kModeF32) {
+      int64_t pq = a[0], pe = a[1];
+      if constexpr (PA == 2) {
+        pq = pq * 256 + a[2];
+        pe = pe * 256 + a[3];
+      }
+      T = mq * pq + pe + beff;
+    } else if constexpr (MODE == kModeExact) {
+      int64_t pq = a[0];
+      if constexpr (PA == 2) pq = pq * 256 + a[1];
+      T = pq + beff;
+    } else {
+      T = static_cast<int64_t>(a[0]) * 65536 + static_cast<int64_t>(a[1]) * 256 + a[2] + beff;
+    }
+    bool near = false;
+    int64_t fl = 0;
+    int32_t code = requant_fast96(T, cmn, tn, p.zp_out, p.qmax, &near, &fl);
+    if (near) code = requant_tie(T, fl, mul, es + p.act_exp2, p.act_mant, p.out_mant, p.out_exp2, p.zp_out, p.qmax);
+    if (u16)
+      reinterpret_cast<uint16_t*>(p.out)[static_cast<size_t>(tok) * p.N + n] = static_cast<uint16_t>(code);
+    else
+      reinterpret_cast<uint8_t*>(p.out)[static_cast<size_t>(tok) * p.N + n] = static_cast<uint8_t>(code);
+  };
+
+  if (splits == 1) {
+    // ---------------------------------------------------------------- whole K here: TMEM -> requant
+    if (ch_ok) {
+#pragma unroll 1
+      for (int t0 = 0; t0 < MP && t0 < p.M; t0 += 16) {
+        uint32_t v[NA][16];
+#pragma unroll
+        for (int g = 0; g < NA; ++g) tmem_ld16(tl + g * MP + t0, v[g]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (t0 + j >= p.M) break;
+          int32_t a[NA];
+#pragma unroll
+          for (int g = 0; g < NA; ++g) a[g] = ok ? static_cast<int32_t>(v[g][j]) : 0;
+          emit(t0 + j, a);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- K split over the cluster:
+    // every CTA parks its int32 partials [acc][tok][ch] in its own shared memory, then CTA r sums
+    // tokens [r*MP/S, (r+1)*MP/S) over all CTAs (distributed shared memory) and requantizes them.
+    if (is_epi) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < NA * MP; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tl + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) red[(c0 + j) * 128 + ch_local] = ok ? static_cast<int32_t>(v[j]) : 0;
+      }
+    }
+    cluster_sync();  // every CTA's partials are visible cluster-wide
+    if (ch_ok) {
+      const int per = MP / splits;
+      const int tb = static_cast<int>(crank) * per;
+      const uint32_t red_s = smem_u32(red);
+#pragma unroll 1
+      for (int tok = tb; tok < tb + per && tok < p.M; ++tok) {
+        int32_t a[NA];
+#pragma unroll
+        for (int g = 0; g < NA; ++g) a[g] = 0;
+        // all loads of this token first (independent), then the sums
+#pragma unroll 1
+        for (int r = 0; r < splits; ++r) {
+          const uint32_t base = map_to_rank(red_s, static_cast<uint32_t>(r)) + static_cast<uint32_t>((tok * 128 + ch_local) * 4);
+          int32_t v[NA];
+#pragma unroll
+          for (int g = 0; g < NA; ++g) v[g] = ld_cluster_s32(base + static_cast<uint32_t>(g * MP * 128 * 4));
+#pragma unroll
+          for (int g = 0; g < NA; ++g) a[g] += v[g];
+        }
+        emit(tok, a);
+      }
+    }
+    cluster_sync();  // no CTA leaves while others may still read its partials
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+int sm_count_dec() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// K splits: enough CTAs to cover the SMs, each keeping at least 4 K blocks, at most 8 (portable
+// cluster size), and only where the partial-sum area fits in shared memory.
+int choose_splits(int n_tiles, int kblocks) {
+  const int sms = sm_count_dec();
+  int s = 1;
+  while (s < 8 && n_tiles * (s * 2) <= sms + sms / 4 && kblocks / (s * 2) >= 4) s *= 2;
+  return s;
+}
+
+template <int MODE, int PA, int MP>
+cudaError_t launch_dec(const CUtensorMap& tx, const CUtensorMap& tw, DecodeParams prm, int n_tiles,
+                       cudaStream_t stream) {
+  using Cfg = DecCfg<MODE, PA, MP>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(qdecode_kernel<MODE, PA, MP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::kSmem);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  prm.splits = choose_splits(n_tiles, prm.kblocks);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * prm.splits), 1, 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(prm.splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qdecode_kernel<MODE, PA, MP>, tx, tw, prm);
+}
+
+template <int MODE, int PA>
+cudaError_t launch_dec_mp(int mp, const CUtensorMap& tx, const CUtensorMap& tw, const DecodeParams& prm,
+                          int n_tiles, cudaStream_t stream) {
+  switch (mp) {
+    case 16: return launch_dec<MODE, PA, 16>(tx, tw, prm, n_tiles, stream);
+    case 32: return launch_dec<MODE, PA, 32>(tx, tw, prm, n_tiles, stream);
+    case 64: return launch_dec<MODE, PA, 64>(tx, tw, prm, n_tiles, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+bool decode_supported(const QhtpMatmulPlan* plan, uint32_t m) {
+  if (m == 0 || m > kDecodeMaxM) return false;
+  if (plan->mode == kModeW16 && plan->a_planes != 2) return false;
+  return true;
+}
+
+cudaError_t launch_decode(const GemmLaunch& g, const uint8_t* a_base) {
+  const QhtpMatmulPlan* pl = g.plan;
+  const int mp = g.m <= 16 ? 16 : (g.m <= 32 ? 32 : 64);
+  CUtensorMap tx, tw;
+  const uint64_t x_rows = static_cast<uint64_t>(g.m) * pl->a_planes;
+  if (!make_tmap_2d_u8(&tx, a_base, pl->k, x_rows, pl->k, kTileK, static_cast<uint32_t>(mp)))
+    return cudaErrorInvalidValue;
+  const uint8_t* planes = static_cast<const uint8_t*>(pl->prepared);
+  if (!make_tmap_planes(&tw, pl)) return cudaErrorInvalidValue;
+  DecodeParams prm;
+  prm.M = static_cast<int>(g.m);
+  prm.N = static_cast<int>(pl->n);
+  prm.kblocks = static_cast<int>(pl->k_pad / kTileK);
+  prm.splits = 1;
+  prm.rec = reinterpret_cast<const ChannelRecord*>(planes + pl->plane_bytes);
+  prm.out = g.out;
+  prm.zp_out = pl->out_zp;
+  prm.qmax = pl->out_qmax;
+  prm.act_mant = pl->act_mant;
+  prm.out_mant = pl->out_mant;
+  prm.act_exp2 = pl->act_exp2;
+  prm.out_exp2 = pl->out_exp2;
+  prm.err = g.err;
+  const int n_tiles = static_cast<int>(pl->n_tiles);
+  switch (pl->mode * 2 + (pl->a_planes - 1)) {
+    case kModeF32 * 2 + 0: return launch_dec_mp<kModeF32, 1>(mp, tx, tw, prm, n_tiles, g.stream);
+    case kModeF32 * 2 + 1: return launch_dec_mp<kModeF32, 2>(mp, tx, tw, prm, n_tiles, g.stream);
+    case kModeExact * 2 + 0: return launch_dec_mp<kModeExact, 1>(mp, tx, tw, prm, n_tiles, g.stream);
+    case kModeExact * 2 + 1: return launch_dec_mp<kModeExact, 2>(mp, tx, tw, prm, n_tiles, g.stream);
+    case kModeW16 * 2 + 1: return launch_dec_mp<kModeW16, 2>(mp, tx, tw, prm, n_tiles, g.stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace qhtp

@@ -57,7 +57,7 @@ static PFN_encodeTiled get_encode_fn() {
 }
 
 bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t rows,
-                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   PFN_encodeTiled enc = get_encode_fn();
   if (enc == nullptr) return false;
   cuuint64_t dims[2] = {inner, rows};
@@ -65,13 +65,21 @@ bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 bool make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
                      uint32_t box_inner, uint32_t box_rows) {
   return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, inner, rows, row_stride_bytes, box_inner, box_rows);
+}
+
+// The prepared weight planes as [n_tiles * kblocks * b_rows, 128] bytes: each (tile, K block) is one
+// contiguous, already swizzled operand image, copied verbatim (no TMA swizzle) into a stage.
+bool make_tmap_planes(CUtensorMap* map, const QhtpMatmulPlan* plan) {
+  const uint64_t rows = static_cast<uint64_t>(plan->n_tiles) * (plan->k_pad / kTileK) * b_rows_for_mode(plan->mode);
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, plan->prepared, kTileK, rows, kTileK, kTileK,
+                      b_rows_for_mode(plan->mode), CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 static int sm_count() {
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile % p.m_tiles) * kTileM;
-        const int nb = (tile / p.m_tiles) * Cfg::kBRows;
+        const int nt = tile / p.m_tiles;
         for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -193,7 +201,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int pl = 0; pl < PA; ++pl)
             tma_load_2d(st + pl * Cfg::kStageA, &tmA, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
-          tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], kb * kTileK, nb);
+          tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], 0, (nt * p.kblocks + kb) * Cfg::kBRows);
         }
       }
     }
@@ -434,12 +442,11 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
     a_base = static_cast<const uint8_t*>(g.act);
     a_rows = g.m;
   }
+  if (decode_supported(pl, g.m)) return launch_decode(g, a_base);
   if (!make_tmap_2d_u8(&ta, a_base, K, a_rows, K, kTileK, kTileM)) return cudaErrorInvalidValue;
   const uint32_t brows = b_rows_for_mode(pl->mode);
   const uint8_t* planes = static_cast<const uint8_t*>(pl->prepared);
-  if (!make_tmap_2d_u8(&tb, planes, pl->k_pad, static_cast<uint64_t>(pl->n_tiles) * brows, pl->k_pad, kTileK,
-                       brows))
-    return cudaErrorInvalidValue;
+  if (!make_tmap_planes(&tb, pl)) return cudaErrorInvalidValue;
   GemmParams prm;
   prm.M = static_cast<int>(g.m);
   prm.N = static_cast<int>(pl->n);
@@ -503,10 +510,12 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const uint32_t n = static_cast<uint32_t>(idx / chunks);
     const uint32_t k0 = static_cast<uint32_t>(idx % chunks) * 16;
-    const uint32_t tile = n / kTileN;
-    const size_t row = static_cast<size_t>(tile) * p.b_rows + (n % kTileN);
-    int8_t* r0 = p.planes + row * p.k_pad + k0;
-    int8_t* r1 = r0 + static_cast<size_t>(128) * p.k_pad;  // second plane (f32 / W16 modes)
+    // blocked, pre-swizzled layout: (tile, K block) -> b_rows x 128-byte operand image, row r's
+    // 16-byte chunk c at r*128 + ((c ^ r) & 7)*16
+    const uint32_t tile = n / kTileN, rr = n % kTileN, kb = k0 / kTileK, c = (k0 % kTileK) / 16;
+    const size_t blk = (static_cast<size_t>(tile) * (p.k_pad / kTileK) + kb) * p.b_rows * kTileK;
+    int8_t* r0 = p.planes + blk + rr * kTileK + (((c ^ rr) & 7u) << 4);
+    int8_t* r1 = r0 + 128 * kTileK;  // second plane (f32 / W16 modes): rows 128..255 of the image
     long long sq = 0, se = 0;
     if (p.mode == kModeF32) {
       const uint32_t bits = __float_as_uint(scale[n]);
