@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the quantized-MatMul hot path (and the GDN chunk inverse) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemm|gdn]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemm|gdn|decode]
 
 Headline workload: W4A16 LPBQ GEMM, M=4096, K=4096, N=14336, LPBQ block 64, u16
 activations from N(0,1), int4 weights from N(0,0.02), int32 bias, u16 output.  A "step" is one
@@ -10,8 +10,14 @@ quantized GEMM over one batch of synthetic input.  Metric: logical TOPS = 2*M*N*
 Multi-GPU (torchrun): the GEMM shards over N -- every rank owns a 14336-wide slab of output
 channels (its own weights), so per-GPU work is fixed ("weak" scaling) and no collective touches
 the data path; ``--allgather`` additionally gathers the outputs with NCCL and reports that time
-separately.  Timing: CUDA events on the launching stream, per step, L2 flushed between steps,
-max over ranks.
+separately.  Timing: CUDA events on the launching stream, per step, L2 flushed between steps (a
+256 MB write, then a 256 MB read of another buffer so the write-back happens before the timed
+window), max over ranks.
+
+The default line also carries the GDN C=256 inverse ("secondary", 4096 chunks) and the BASELINE
+decode/prefill rows of the W4A16 LPBQ GEMM ("decode": M in {1, 16, 128}, N in {4096, 14336}, GB/s
+against the HBM peak).  ``--workload gdn`` and ``--workload decode --m M --n N`` run one of those
+alone (the commands the committed ncu summaries were taken with).
 """
 from __future__ import annotations
 
@@ -196,7 +202,22 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
-def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, stream, clk=None) -> list[float]:
+class L2Flush:
+    """Evicts L2 between timed steps: writes a 256 MB buffer (the flush proper), then reads a second
+    256 MB buffer so that the dirty lines of the write are written back here, outside the timed
+    window, and the timed kernel starts from a cold, clean L2 (126 MB)."""
+
+    def __init__(self, device):
+        self.w = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.sink = torch.zeros((), dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.add_(1)
+        torch.amax(self.r, dim=0, out=self.sink)
+
+
+def timed_steps(fn, steps: int, warmup: int, flush, world: int, stream, clk=None) -> list[float]:
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -205,7 +226,7 @@ def timed_steps(fn, steps: int, warmup: int, flush: torch.Tensor, world: int, st
     t_host0 = time.perf_counter()
     times = []
     for _ in range(steps):
-        flush.add_(1)                      # evict L2 (256 MB write) outside the timed window
+        flush()                            # evict L2 outside the timed window
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -302,7 +323,7 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     op = QuantMatMul("w4a16", d["w_packed"], d["scale"], d["bias_q"], act_scale=d["s_a"], out_scale=d["s_o"],
                      schema="lpbq", lpbq_block_scale=d["factor"], lpbq_block=blk)
     act, out = d["act"], torch.empty((m, n), dtype=torch.uint16, device=dev)
-    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev)
     fn = lambda: op(act, out)
     with ClockSampler(local) as clk:
         times = timed_steps(fn, args.steps, args.warmup, flush, world, stream, clk)
@@ -334,7 +355,7 @@ def run_gemm(args, world, rank, local, stream) -> dict:
         "data": "synthetic (BASELINE.json distributions, generated on device)",
         "config": {"workload": "W4A16 LPBQ GEMM (BASELINE configs[2]/[4] shape)", "m": m, "k": k,
                    "n_per_gpu": n, "lpbq_block": blk, "parallelism": f"N-shard x{world}, no data-path collective",
-                   "l2": "256 MB write between steps (flush)", "bit_exact": True},
+                   "l2": "flushed between steps: 256 MB write, then 256 MB read of another buffer (cold, clean L2)", "bit_exact": True},
         "e2e": {"value": ops * world / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
                 "d2h_bytes_per_step": m * n * 2},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
@@ -358,7 +379,44 @@ def run_gemm(args, world, rank, local, stream) -> dict:
         res["cpu_baseline"] = cpu_gemm_baseline(d)
     if not args.no_gdn:
         res["secondary"] = run_gdn(args, world, rank, local, stream, secondary=True)
+    if not args.no_decode:
+        res["decode"] = {"workload": "W4A16 LPBQ decode/prefill rows (BASELINE configs[2])",
+                         "peak_gbs": peaks()["hbm_gbs"], "rows": run_decode(args, world, rank, local, stream)}
     return res
+
+
+def run_decode(args, world, rank, local, stream, shapes=None) -> list:
+    """BASELINE decode/prefill rows of the W4A16 LPBQ GEMM (M in {1, 16, 128}, K = 4096,
+    N in {4096, 14336}): HBM-bound.  Reports GB/s on the algorithmic bytes (int4 weights, block
+    factors, scales, bias, u16 activation and output) and on the bytes the kernel reads (the
+    prepared byte planes: q and the float32-dequant residual e', 2 bytes per weight)."""
+    from qcom_htp_b200 import QuantMatMul
+    dev = torch.device("cuda", local)
+    pk = peaks()
+    flush = L2Flush(dev)
+    rows = []
+    k, blk = 4096, 64
+    shapes = shapes or [(m, n) for n in (4096, 14336) for m in (1, 16, 128)]
+    for m, n in shapes:
+        if True:
+            d = synth_w4a16_lpbq(m, k, n, blk, seed=4321 + m + n, device=dev)
+            op = QuantMatMul("w4a16", d["w_packed"], d["scale"], d["bias_q"], act_scale=d["s_a"],
+                             out_scale=d["s_o"], schema="lpbq", lpbq_block_scale=d["factor"], lpbq_block=blk)
+            act, out = d["act"], torch.empty((m, n), dtype=torch.uint16, device=dev)
+            times = timed_steps(lambda: op(act, out), max(5, args.steps // 2), args.warmup, flush, world, stream)
+            op.check_device(m)
+            t = max_over_ranks(statistics.median(times), world)
+            alg = m * k * 2 + n * k // 2 + n * (k // blk) + n * 8 + m * n * 2
+            read = int(op.plan.plane_bytes) + n * 32 + m * k * 2 + m * n * 2
+            rows.append({"m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
+                         "kernel": "qdecode_kernel (channel-major, cluster split-K)" if m <= 64 else
+                                   "qgemm_kernel (row tiles)",
+                         "alg_bytes": alg, "alg_gbs": round(alg / t / 1e9, 1),
+                         "alg_frac": round(alg / t / 1e9 / pk["hbm_gbs"], 3),
+                         "read_bytes": read, "read_gbs": round(read / t / 1e9, 1),
+                         "read_frac": round(read / t / 1e9 / pk["hbm_gbs"], 3)})
+            del op, d, act, out
+    return rows
 
 
 def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
@@ -368,7 +426,7 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
     n_chunks = args.gdn_chunks
     A = synth_gdn_A(n_chunks, C, 128, seed=99 + rank, device=dev)
     T = torch.empty((n_chunks, C, C), dtype=torch.float32, device=dev)
-    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev)
     fn = lambda: gdn_inverse(A, T)
     steps = args.steps
     with ClockSampler(local) as clk:
@@ -426,13 +484,14 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gdn"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "gdn", "decode"], default="gemm")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--n", type=int, default=14336)
     ap.add_argument("--gdn-chunks", type=int, default=4096)
     ap.add_argument("--allgather", action="store_true")
     ap.add_argument("--no-gdn", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -444,8 +503,24 @@ def main() -> int:
         return 0
     world, rank, local = dist_init()
     stream = torch.cuda.current_stream()
-    res = run_gemm(args, world, rank, local, stream) if args.workload == "gemm" else \
-        run_gdn(args, world, rank, local, stream)
+    if args.workload == "gemm":
+        res = run_gemm(args, world, rank, local, stream)
+    elif args.workload == "gdn":
+        res = run_gdn(args, world, rank, local, stream)
+    else:
+        # one decode-shaped GEMM (the --m / --n shape, K = 4096), HBM roofline
+        row = run_decode(args, world, rank, local, stream, shapes=[(args.m, args.n)])[0]
+        pk = peaks()
+        res = {"metric": "w4a16_lpbq_decode_gbs", "value": row["alg_gbs"] * world, "unit": "GB/s",
+               "n_gpus": world, "steps": max(5, args.steps // 2), "warmup": args.warmup,
+               "ms_per_step": row["us"] * 1e-3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "dtype": "u16xint4->u16 (int8 tensor ops, int64 combine)", "data": "synthetic (BASELINE.json distributions)",
+               "config": {"workload": f"W4A16 LPBQ decode M={args.m} K=4096 N={args.n}", "m": args.m, "k": 4096,
+                          "n": args.n, "l2": "flushed between steps (256 MB write + 256 MB read)"},
+               "roofline": {"bound": "hbm", "achieved": row["alg_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": row["alg_frac"], "traffic": None, "read_gbs": row["read_gbs"],
+                            "read_frac": row["read_frac"], "kernel": row["kernel"]},
+               "gpu_launches": 2 * max(5, args.steps // 2), "e2e": None}
     if rank == 0:
         print(json.dumps(res))
     if world > 1:

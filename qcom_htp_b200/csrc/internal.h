@@ -53,7 +53,7 @@ void set_last_message(const char* msg);
 cudaError_t launch_gemm(const GemmLaunch& g);
 // qdecode.cu: channel-major (swap-AB) kernel for M <= kDecodeMaxM activation rows; a_base is the
 // u8 activation or the [hi; lo] byte planes of a u16 activation
-constexpr uint32_t kDecodeMaxM = 64;
+constexpr uint32_t kDecodeMaxM = 128;
 bool decode_supported(const QhtpMatmulPlan* plan, uint32_t m);
 cudaError_t launch_decode(const GemmLaunch& g, const uint8_t* a_base);
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,

@@ -1,8 +1,9 @@
-"""Decode-shaped GEMM (M <= 64 activation rows): the channel-major kernel with a cluster K split.
+"""Decode-shaped GEMM (M <= 128 activation rows): the channel-major kernel with a cluster K split.
 
 Every output byte must equal the oracle's (bit-exact), for each family and dequant mode, at row
-counts on both sides of the 16/32/64-column instruction shapes and of the row-tiled kernel's
-threshold (M = 65), with K split over up to 8 CTAs of a cluster and ragged channel tiles.
+counts on both sides of the 16/32/64/128-column instruction shapes and of the row-tiled kernel's
+threshold (M = 129), with K split over up to 8 CTAs of a cluster (reduced in rounds of 64 rows)
+and ragged channel tiles.
 """
 import numpy as np
 import pytest
@@ -16,7 +17,7 @@ FAMS = ["u8i8", "w4a8_per_channel", "w4a8_lpbq", "w8a16", "w4a16_per_channel", "
 
 
 @pytest.mark.parametrize("family", FAMS)
-@pytest.mark.parametrize("m", [1, 2, 16, 33, 64, 65])
+@pytest.mark.parametrize("m", [1, 2, 16, 33, 64, 65, 100, 128, 129])
 def test_decode_rows_bit_exact(family, m):
     # K = 2048 -> 16 K blocks: split 4 ways over a cluster; N = 256 -> two channel tiles
     c = O.generate_case(family, "normal_random", m, 2048, 256)
@@ -43,7 +44,7 @@ def test_decode_exact_dequant_mode(family):
     np.testing.assert_array_equal(run_case(c, dequant="exact"), O.exact_output(c, dequant="exact"))
 
 
-@pytest.mark.parametrize("m", [1, 16, 64])
+@pytest.mark.parametrize("m", [1, 16, 64, 128])
 def test_decode_w16a16(m):
     c = make_w16a16_case(m, 1024, 160, seed=0x16 + m)
     np.testing.assert_array_equal(run_case(c), O.exact_output(c, dequant="exact"))
