@@ -38,10 +38,13 @@ sys.path.insert(0, str(ROOT))
 L2_FLUSH_BYTES = 256 << 20
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from one
-# `ncu --set full` capture of this script's own workload (bench.py --steps 1 --warmup 3 ...)
+# `ncu --set full` capture of this script's own workload (bench.py --steps 1 --warmup 3 ...); the
+# GDN figure is a 1024-chunk capture scaled by the chunk count to the 4096-chunk launch
 NCU_TRAFFIC_BYTES = {
-    ("qgemm", 4096, 4096, 14336): 153_884_160 + 100_395_264,
-    ("gdn", 4096): 337_263_104 + 1_020_883_000,
+    ("qgemm", 4096, 4096, 14336): 155_152_640 + 101_383_680,          # full-size capture
+    ("gdn", 4096): 4 * (100_822_016 + 208_797_696),                    # 1024-chunk capture x 4 chunks
+    ("qdecode", 16, 4096, 14336): 118_095_360 + 3_455_744,             # full-size capture
+    ("qdecode", 1, 4096, 4096): 33_754_112 + 0,                        # full-size capture
 }
 
 
@@ -409,8 +412,7 @@ def run_decode(args, world, rank, local, stream, shapes=None) -> list:
             alg = m * k * 2 + n * k // 2 + n * (k // blk) + n * 8 + m * n * 2
             read = int(op.plan.plane_bytes) + n * 32 + m * k * 2 + m * n * 2
             rows.append({"m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
-                         "kernel": "qdecode_kernel (channel-major, cluster split-K)" if m <= 64 else
-                                   "qgemm_kernel (row tiles)",
+                         "kernel": "split_u16_planes + qdecode_kernel (channel-major, cluster split-K)",
                          "alg_bytes": alg, "alg_gbs": round(alg / t / 1e9, 1),
                          "alg_frac": round(alg / t / 1e9 / pk["hbm_gbs"], 3),
                          "read_bytes": read, "read_gbs": round(read / t / 1e9, 1),
@@ -518,7 +520,8 @@ def main() -> int:
                "config": {"workload": f"W4A16 LPBQ decode M={args.m} K=4096 N={args.n}", "m": args.m, "k": 4096,
                           "n": args.n, "l2": "flushed between steps (256 MB write + 256 MB read)"},
                "roofline": {"bound": "hbm", "achieved": row["alg_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
-                            "frac": row["alg_frac"], "traffic": None, "read_gbs": row["read_gbs"],
+                            "frac": row["alg_frac"], "traffic": NCU_TRAFFIC_BYTES.get(("qdecode", args.m, 4096, args.n)),
+                            "read_gbs": row["read_gbs"],
                             "read_frac": row["read_frac"], "kernel": row["kernel"]},
                "gpu_launches": 2 * max(5, args.steps // 2), "e2e": None}
     if rank == 0:
