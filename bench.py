@@ -444,6 +444,19 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
                         "frac": achieved / pk["hbm_gbs"], "traffic": NCU_TRAFFIC_BYTES.get(("gdn", n_chunks)),
                         "peak_src": f"hbm_gbs ({pk['src']})"},
            "gpu_launches": steps, "clocks": clk.summary()}
+    # the reference's production carrier (GdnSolve / gdnbm_solve): u16 codes in and out, scales of
+    # gdn_solve_oc_check.py:20-23, same chunks
+    from qcom_htp_b200 import gdn_solve_u16
+    sA, sT, zp = 2.770166930875267e-05, 6.103701895199438e-05, 32768
+    Ac = torch.clamp(torch.round(A.float() / sA) + zp, 0, 65535).to(torch.int32).to(torch.uint16)
+    Tc = torch.empty_like(Ac)
+    fn16 = lambda: gdn_solve_u16(Ac, zpA=zp, sA=sA, zpT=zp, sT=sT, out=Tc)
+    t16 = max_over_ranks(statistics.mean(timed_steps(fn16, steps, args.warmup, flush, world, stream)), world)
+    b16 = n_chunks * (C * C * 2 + C * C * 2)
+    res["u16_carrier"] = {"metric": "gdn_solve_u16_chunks_per_s", "value": n_chunks * world / t16,
+                          "ms_per_step": t16 * 1e3, "hbm_gbs": b16 / t16 / 1e9, "hbm_frac": b16 / t16 / 1e9 / pk["hbm_gbs"],
+                          "note": "u16 codes A -> u16 codes T (zp 32768), algorithmic bytes 2C^2 + 2C^2 per chunk"}
+    del Ac, Tc
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_gdn_baseline(A)
     if not secondary:

@@ -474,6 +474,7 @@ cudaError_t launch_gdn_bf16(const void* A, float* T, int64_t n_chunks, int C, cu
 
 cudaError_t launch_gdn_u16(const uint16_t* A, int64_t n_chunks, int C, int zpA, float sA, int zpT, float sT,
                            uint16_t* T, cudaStream_t stream) {
+  if (C == 256 && gdn256_supported(A, T, n_chunks)) return launch_gdn256_u16(A, n_chunks, zpA, sA, zpT, sT, T, stream);
   GdnIO io{A, T, n_chunks, zpA, zpT, sA, 1.0f / sT, nullptr};
   return launch_any<true>(io, C, stream);
 }

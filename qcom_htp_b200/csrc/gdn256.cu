@@ -1,5 +1,6 @@
 // GDN / KDA chunk triangular inverse for C = 256 on B200:  T = (I - A)^-1 per chunk, A strictly
-// lower triangular, bf16 in, f32 out.
+// lower triangular; bf16 in / f32 out, or the u16 code carrier of GdnSolve / gdnbm_solve (value =
+// (code - zp) * scale, example/gdn_native/solve_op/src/GdnSolveOp.cpp:195-281, gdnbm.idl:10-12).
 //
 // Same algorithm family as the reference's block solvers (example/gdn_native/solve_op/
 // gdn_solve_ref.c:19-69 forward substitution + block merge; solve_br_op block recursion): the
@@ -56,7 +57,7 @@ constexpr uint32_t kRS2 = 128 * KB;      //     [RS1; RS3], [RS2; L2R1] and [0; 
 constexpr uint32_t kL2R1 = 136 * KB;
 constexpr uint32_t kRS1 = 144 * KB;
 constexpr uint32_t kRS3 = 152 * KB;
-constexpr uint32_t kZero = 160 * KB;     // 32x32 f32 zero tile (source of the upper-triangle stores)
+constexpr uint32_t kZero = 160 * KB;     // 32x32 zero tile of the output type (upper-triangle stores)
 constexpr uint32_t kBar = 164 * KB;
 constexpr uint32_t kSmemBytes = kBar + 64 + 1024;  // barriers + alignment slack
 
@@ -88,11 +89,60 @@ __device__ __forceinline__ void put_row_bf16(uint8_t* img, int r, int c0, const 
   }
 }
 
-// 32 consecutive f32 values of row r -> a 32x32 f32 staging tile (same swizzle as the T tensor map).
-__device__ __forceinline__ void put_row_f32(uint8_t* tile, int r, const uint32_t (&v)[32]) {
+struct OutCodes {   // u16 output carrier: code = clip(rint(t / sT) + zpT, 0, 65535)
+  float inv_sT, zpT;
+};
+
+__device__ __forceinline__ uint32_t to_code(float t, const OutCodes& oc) {
+  const float q = fminf(fmaxf(rintf(t * oc.inv_sT) + oc.zpT, 0.0f), 65535.0f);
+  return static_cast<uint32_t>(q);
+}
+
+// 32 consecutive f32 values of row r -> a 32x32 staging tile of the output type, in the swizzle of
+// the T tensor map: f32 rows of 128 bytes with the 128-byte swizzle, or u16 code rows of 64 bytes
+// with the 64-byte swizzle (16-byte chunk c at ((c ^ (r >> 1)) & 3) * 16).
+template <bool U16>
+__device__ __forceinline__ void put_row_out(uint8_t* tile, int r, const uint32_t (&v)[32], const OutCodes& oc) {
+  if constexpr (U16) {
 #pragma unroll
-  for (int c = 0; c < 8; ++c)
-    *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    for (int c = 0; c < 4; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        w[i] = to_code(__uint_as_float(v[8 * c + 2 * i]), oc) | (to_code(__uint_as_float(v[8 * c + 2 * i + 1]), oc) << 16);
+      *reinterpret_cast<uint4*>(tile + r * 64 + (((c ^ (r >> 1)) & 3) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+}
+
+// Input element pair -> f32: bf16 bits, or u16 codes (value = (code - zpA) * sA).
+struct InCodes {
+  float sA;
+  int zpA;  // value = (code - zpA) * sA: exact integer difference, one rounding
+};
+
+template <bool U16>
+__device__ __forceinline__ float in_lo(uint32_t w, const InCodes& ic) {
+  if constexpr (U16) return static_cast<float>(static_cast<int>(w & 0xFFFFu) - ic.zpA) * ic.sA;
+  return __uint_as_float(w << 16);
+}
+template <bool U16>
+__device__ __forceinline__ float in_hi(uint32_t w, const InCodes& ic) {
+  if constexpr (U16) return static_cast<float>(static_cast<int>(w >> 16) - ic.zpA) * ic.sA;
+  return __uint_as_float(w & 0xFFFF0000u);
+}
+
+// u16 codes -> bf16 values in place, 16 bytes (8 elements) at a time.
+__device__ __forceinline__ void codes_to_bf16(uint8_t* p, const InCodes& ic) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = pack_bf16(in_lo<true>(w[i], ic), in_hi<true>(w[i], ic));
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // Level 0: forward substitution on one 32x32 diagonal block held in a swizzled bf16 tile (rows 0..31,
@@ -100,7 +150,9 @@ __device__ __forceinline__ void put_row_f32(uint8_t* tile, int r, const uint32_t
 //     t[i] = delta(i, j) + sum_{k<i} A[i][k] * t[k]
 // with two partial sums (even / odd k) to halve the dependency chain.  Entries with k >= i are
 // never read.  t[i] is exactly 0 for i < j and exactly 1 for i == j.
-__device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off, int lane, float (&t)[32]) {
+template <bool U16>
+__device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off, int lane, float (&t)[32],
+                                             const InCodes& ic) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     float s0 = (i == lane) ? 1.0f : 0.0f, s1 = 0.0f;
@@ -113,7 +165,7 @@ __device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off,
         for (int e = 0; e < 8; ++e) {
           const int k = 8 * c + e;
           if (k < i) {
-            const float a = (e & 1) ? __uint_as_float(w[e >> 1] & 0xFFFF0000u) : __uint_as_float(w[e >> 1] << 16);
+            const float a = (e & 1) ? in_hi<U16>(w[e >> 1], ic) : in_lo<U16>(w[e >> 1], ic);
             if (e & 1)
               s1 = fmaf(a, t[k], s1);
             else
@@ -149,14 +201,17 @@ __device__ __forceinline__ void zero_box(int e, int& x, int& y) {
 }
 
 struct Gdn256Args {
-  float* T;
+  void* T;
+  InCodes ic;
+  OutCodes oc;
   int64_t n_chunks;
   int* err;
 };
 
+template <bool U16>
 __global__ void __launch_bounds__(kThreads, 1)
-    gdn256_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmT,
-                       const Gdn256Args args) {
+    gdn256_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmT,
+                  const Gdn256Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(sm);
@@ -167,7 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = warp & 3, half = warp >> 2;  // TMEM lane quadrant, column half
   int* err = args.err;
-  float* T = args.T;
+  void* T = args.T;
+  const InCodes ic = args.ic;
+  const OutCodes oc = args.oc;
   const int64_t n_chunks = args.n_chunks;
 
   if (tid == 0) {
@@ -180,7 +237,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmT);
   }
   for (int e = tid; e < static_cast<int>(kTile / 16); e += kThreads)
-    reinterpret_cast<uint4*>(sm + kZero)[e] = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (U16) {
+      const uint32_t z = to_code(0.0f, oc) * 0x10001u;
+      reinterpret_cast<uint4*>(sm + kZero)[e] = make_uint4(z, z, z, z);
+    } else {
+      reinterpret_cast<uint4*>(sm + kZero)[e] = make_uint4(0u, 0u, 0u, 0u);
+    }
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
@@ -253,12 +315,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q = warp >> 1, odd = warp & 1;
       const uint8_t* src = aul + (odd ? kAL : kAU) + q * kTile;
       float t[32];
-      solve_diag32(src, odd * 4, lane, t);
+      solve_diag32<U16>(src, odd * 4, lane, t, ic);
       __syncwarp();  // all lanes are done reading `src` before odd blocks overwrite it below
-      // f32 result rows (coalesced: lane j writes column 32w + j of row 32w + i)
-      float* out = T + static_cast<int64_t>(y0 + 32 * warp) * kC + 32 * warp + lane;
+      // result rows (coalesced: lane j writes column 32w + j of row 32w + i)
+      const int64_t o0 = static_cast<int64_t>(y0 + 32 * warp) * kC + 32 * warp + lane;
+      if constexpr (U16) {
+        uint16_t* out = static_cast<uint16_t*>(T) + o0;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) out[static_cast<int64_t>(i) * kC] = t[i];
+        for (int i = 0; i < 32; ++i) out[static_cast<int64_t>(i) * kC] = static_cast<uint16_t>(to_code(t[i], oc));
+      } else {
+        float* out = static_cast<float*>(T) + o0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[static_cast<int64_t>(i) * kC] = t[i];
+      }
       // bf16 row image of the 64x64 block T_q: this block at rows/columns 32*odd..
       uint8_t* rs = sm + rs_off(q);
       const int cc = 32 * odd + lane;
@@ -279,6 +348,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int m = 0; m < 4; ++m)
           *reinterpret_cast<uint4*>(rs + swz(8 * m + (lane >> 2), 4 + (lane & 3))) = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (U16) {
+          // A10_q (columns 0..31 of AL[q]) feeds the level-1 MMA: codes -> bf16 in place
+          uint8_t* al = aul + kAL + q * kTile;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) codes_to_bf16(al + swz(8 * m + (lane >> 2), lane & 3), ic);
+        }
       }
     }
     if (tid == 0 && ok) pend[buf] = false;
@@ -306,6 +381,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64 * warp, v);
       tmem_ld_wait();
       put_row_bf16(aul + kAU + warp * kTile, lane, 0, v);
+    } else if constexpr (U16) {
+      // warps 4..7 are free here: the level-2 and level-3 A operands (A2 16 KB, A3 32 KB), u16 codes
+      // -> bf16 in place, once their loads have landed
+      if (ok) ok = mbar_wait(ld23_bar, it & 1, err, kErrTimeoutFull);
+      if (ok)
+        for (int e = tid - 128; e < static_cast<int>(48 * KB / 16); e += 128) codes_to_bf16(sm + kA2 + 16 * e, ic);
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -333,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
       put_row_bf16(sm + rs_off(warp), 32 + lane, 0, v);
       uint8_t* st = aul + kAU + warp * kTile;  // XB1[q] is dead: the second product has completed
-      put_row_f32(st, lane, v);
+      put_row_out<U16>(st, lane, v, oc);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -350,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) ok = mbar_wait(ld23_bar, it & 1, err, kErrTimeoutFull);
     if (tid == 0 && ok) pend23 = false;
+
     fence_proxy_async_smem();
     tc_fence_before();
     failed = __syncthreads_or(ok ? 0 : 1) != 0;
@@ -402,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* st = warp < 4 ? aul + kAU + warp * kTile : sm + kA2 + (warp - 4) * kTile;
       if (lane == 0) bulk_wait_read_all();
       __syncwarp();
-      put_row_f32(st, lane, v);
+      put_row_out<U16>(st, lane, v, oc);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -471,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         uint8_t* st = j == 0 ? (warp < 4 ? aul + kAU + warp * kTile : sm + kA2 + (warp - 4) * kTile)
                              : (warp < 4 ? aul + kAL + warp * kTile : sm + kRS0 + (warp - 4) * kTile);
-        put_row_f32(st, lane, v);
+        put_row_out<U16>(st, lane, v, oc);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tma_store_2d(&tmT, st, 64 * half + 32 * j, y0 + 128 + 32 * qd);
@@ -510,7 +592,10 @@ bool gdn256_supported(const void* A, const void* T, int64_t n_chunks) {
          n_chunks > 0 && n_chunks <= (int64_t{1} << 23) - 1;
 }
 
-cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaStream_t stream) {
+namespace {
+
+template <bool U16>
+cudaError_t launch_gdn256(const void* A, void* T, int64_t n_chunks, InCodes ic, OutCodes oc, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -522,7 +607,7 @@ cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaSt
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!attr_set[dev]) {
-      e = cudaFuncSetAttribute(gdn256_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      e = cudaFuncSetAttribute(gdn256_kernel<U16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
       if (e != cudaSuccess) return e;
       e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
       if (e != cudaSuccess) return e;
@@ -535,12 +620,27 @@ cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaSt
   }
   CUtensorMap ta, tt;
   const uint64_t rows = static_cast<uint64_t>(n_chunks) * kC;
-  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A, kC, rows, kC * 2, 64, 32)) return cudaErrorInvalidValue;
-  if (!make_tmap_2d(&tt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, T, kC, rows, kC * 4, 32, 32)) return cudaErrorInvalidValue;
+  const CUtensorMapDataType at = U16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap_2d(&ta, at, A, kC, rows, kC * 2, 64, 32)) return cudaErrorInvalidValue;
+  const bool okT = U16 ? make_tmap_2d(&tt, CU_TENSOR_MAP_DATA_TYPE_UINT16, T, kC, rows, kC * 2, 32, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_64B)
+                       : make_tmap_2d(&tt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, T, kC, rows, kC * 4, 32, 32);
+  if (!okT) return cudaErrorInvalidValue;
   const int64_t grid = n_chunks < sms[dev] ? n_chunks : sms[dev];
-  Gdn256Args args{T, n_chunks, err_ptr[dev]};
-  gdn256_bf16_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(ta, tt, args);
+  Gdn256Args args{T, ic, oc, n_chunks, err_ptr[dev]};
+  gdn256_kernel<U16><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(ta, tt, args);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaStream_t stream) {
+  return launch_gdn256<false>(A, T, n_chunks, InCodes{1.0f, 0}, OutCodes{1.0f, 0.0f}, stream);
+}
+
+cudaError_t launch_gdn256_u16(const uint16_t* A, int64_t n_chunks, int zpA, float sA, int zpT, float sT, uint16_t* T,
+                              cudaStream_t stream) {
+  return launch_gdn256<true>(A, T, n_chunks, InCodes{sA, zpA}, OutCodes{1.0f / sT, static_cast<float>(zpT)}, stream);
 }
 
 }  // namespace qhtp

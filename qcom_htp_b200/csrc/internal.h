@@ -65,9 +65,11 @@ cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k,
 cudaError_t launch_gdn_bf16(const void* A, float* T, int64_t n_chunks, int C, cudaStream_t stream);
 cudaError_t launch_gdn_u16(const uint16_t* A, int64_t n_chunks, int C, int zpA, float sA, int zpT, float sT,
                            uint16_t* T, cudaStream_t stream);
-// gdn256.cu: C = 256, tensor-core doubling kernel (bf16 in, f32 out)
+// gdn256.cu: C = 256, tensor-core doubling kernel (bf16 in / f32 out, or u16 codes in / out)
 bool gdn256_supported(const void* A, const void* T, int64_t n_chunks);
 cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaStream_t stream);
+cudaError_t launch_gdn256_u16(const uint16_t* A, int64_t n_chunks, int zpA, float sA, int zpT, float sT, uint16_t* T,
+                              cudaStream_t stream);
 
 // tensor maps (qgemm.cu)
 bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t rows,

@@ -101,3 +101,43 @@ def test_gdnbm_signature_mirror():
     assert G.oc(T, G.inverse_fp64(G.from_codes(Ac, np.float32(sA), zp))) <= G.OC_GATE
     rc, _, _ = gdnbm_solve(Ac.tobytes(), 4, 128, zp, zp, bits(sA), bits(sT), 4)
     assert rc == -1      # the reference's C != 256 contract
+
+
+@pytest.mark.parametrize("n_chunks", [1, 64, 149])
+def test_u16_codes_c256_structure_and_gate(n_chunks):
+    """u16 carrier at C=256 (the tensor-core kernel): upper triangle exactly the zero code, diagonal
+    exactly the code of 1.0, oc against the fp64 inverse of the decoded input within the gate.
+    149 chunks = one more than the 148 persistent CTAs (a second pass for one CTA)."""
+    from qcom_htp_b200 import gdn_solve_u16
+    sA, sT, zp = 2.770166930875267e-05, 6.103701895199438e-05, 32768
+    A = G.make_chunk_A(n_chunks, C=256, seed=0xC0DE + n_chunks, as_bf16=False)
+    Ac = G.to_codes(A, sA, zp)
+    Tc = gdn_solve_u16(torch.from_numpy(Ac).cuda(), zpA=zp, sA=sA, zpT=zp, sT=sT).cpu().numpy()
+    iu = np.triu_indices(256, 1)
+    assert np.all(Tc[:, iu[0], iu[1]] == zp)
+    one = int(np.rint(np.float32(1.0) * np.float32(1.0 / np.float32(sT)))) + zp
+    assert np.all(np.diagonal(Tc, axis1=1, axis2=2) == min(one, 65535))
+    T = G.from_codes(Tc, np.float32(sT), zp)
+    oc = G.oc(T, G.inverse_fp64(G.from_codes(Ac, np.float32(sA), zp)))
+    print(f"u16 C=256 n={n_chunks} oc={oc:.3e}")
+    assert oc <= G.OC_GATE
+
+
+def test_u16_codes_c128_small_kernel():
+    """C=128 u16 (served by the first kernel): same contract."""
+    from qcom_htp_b200 import gdn_solve_u16
+    sA, sT, zp = 2.770166930875267e-05, 6.103701895199438e-05, 32768
+    A = G.make_chunk_A(16, C=128, seed=0x128, as_bf16=False)
+    Ac = G.to_codes(A, sA, zp)
+    Tc = gdn_solve_u16(torch.from_numpy(Ac).cuda(), zpA=zp, sA=sA, zpT=zp, sT=sT).cpu().numpy()
+    T = G.from_codes(Tc, np.float32(sT), zp)
+    assert G.oc(T, G.inverse_fp64(G.from_codes(Ac, np.float32(sA), zp))) <= G.OC_GATE
+
+
+@pytest.mark.parametrize("n_chunks", [1, 149])
+def test_bf16_c256_chunk_counts(n_chunks):
+    from qcom_htp_b200 import gdn_inverse
+    A = G.make_chunk_A(n_chunks, C=256, seed=0xB16 + n_chunks)
+    T = gdn_inverse(_bf16(A)).cpu().numpy()
+    assert G.oc(T, G.inverse_fp64(A)) < 1e-4
+    assert np.all(np.triu(T, 1) == 0)
