@@ -140,8 +140,8 @@ __device__ __forceinline__ uint32_t requant_one(const int32_t (&a)[NA], const Ch
   }
   bool near = false;
   int64_t fl = 0;
-  int32_t code = requant_fast96(T, c.cmn, c.tn, p.zp_out, p.qmax, &near, &fl);
-  if (near) code = requant_tie(T, fl, c.mul, c.es + p.act_exp2, p.act_mant, p.out_mant, p.out_exp2, p.zp_out, p.qmax);
+  int32_t code = requant_fast96s(T, c.cmn, c.tn, p.zp_out, p.qmax, &near, &fl);
+  if (near) code = requant_tie_w(T, fl, c.mul, c.es + p.act_exp2, p.act_mant, p.out_mant, p.out_exp2, p.zp_out, p.qmax);
   return static_cast<uint32_t>(code);
 }
 

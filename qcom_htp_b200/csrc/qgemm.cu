@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int tn = __ldg(reinterpret_cast<const int*>(rec + c0 + j) + 6);
             const uint64_t cmn = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
             bool nr;
-            code[j] = static_cast<uint32_t>(requant_fast96(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
+            code[j] = static_cast<uint32_t>(requant_fast96s(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
             near_mask |= nr ? (1u << j) : 0u;
           }
           if (near_mask != 0) {  // rare: within 2^-29 of a tie -> exact decision
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint32_t ms = (wb & 0x7FFFFFu) | 0x800000u;
                 const int es = static_cast<int>((wb >> 23) & 0xFFu) - 150;
                 const uint32_t mul = MODE == kModeF32 ? 1u : ms;
-                code[j] = static_cast<uint32_t>(requant_tie(T[j], fl[j], mul, es + p.act_exp2, p.act_mant,
+                code[j] = static_cast<uint32_t>(requant_tie_w(T[j], fl[j], mul, es + p.act_exp2, p.act_mant,
                                                             p.out_mant, p.out_exp2, p.zp_out, p.qmax));
               }
             }

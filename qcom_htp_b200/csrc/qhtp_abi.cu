@@ -99,10 +99,10 @@ int32_t qhtp_requant_code_host(int64_t T, uint64_t cm, int32_t cshift, uint32_t 
   // decision near a tie
   const FastConst fc = fast_const(cm, cshift);
   bool near = false;
-  int64_t fl = 0;
-  const int32_t code = requant_fast96(T, fc.cmn, fc.tn, zp_out, qmax, &near, &fl);
+  int64_t w = 0;
+  const int32_t code = requant_fast96s(T, fc.cmn, fc.tn, zp_out, qmax, &near, &w);
   if (!near) return code;
-  return requant_tie(T, fl, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
+  return requant_tie_w(T, w, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax);
 }
 
 QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {

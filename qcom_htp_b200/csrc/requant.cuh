@@ -212,6 +212,44 @@ QHTP_HD int32_t requant_fast96(int64_t T, uint64_t cmn, int tn, int32_t zp_out, 
   return static_cast<int32_t>(r);
 }
 
+// Signed form of requant_fast96 (same constants, same error budget, same tie window).  With
+// ap = T << tn and P = ap * cmn (signed 128-bit), V = P / 2^96 and
+//     W = floor((floor(P / 2^64) + 2^31) / 4) = floor((V + 1/2) * 2^30)   (arithmetic shifts)
+// carries round_half_up(V) in W >> 30 and the 30 fraction bits of V + 1/2 in its low bits for either
+// sign, so no absolute value or re-negation is needed.  Returns clip(round_half_up(V) + zp) and sets
+// *near as requant_fast96 does; *w_out receives W for requant_tie_w.
+QHTP_HD int32_t requant_fast96s(int64_t T, uint64_t cmn, int tn, int32_t zp_out, int32_t qmax, bool* near,
+                                int64_t* w_out) {
+  const int64_t top = T >> (63 - tn);  // 0 or -1 unless |T| >= 2^(63-tn)
+  const bool big = (top != 0) & (top != -1);
+  const int64_t ap = static_cast<int64_t>(static_cast<uint64_t>(T) << tn);
+#ifdef __CUDA_ARCH__
+  const int64_t hi = __mul64hi(ap, static_cast<int64_t>(cmn));
+#else
+  const int64_t hi = static_cast<int64_t>((static_cast<__int128>(ap) * static_cast<__int128>(cmn)) >> 64);
+#endif
+  const int64_t W = (hi + (int64_t{1} << 31)) >> 2;
+  const uint32_t win = static_cast<uint32_t>(W) & 0x3FFFFFFFu;
+  *near = !big && (((win + 2u) & 0x3FFFFFFFu) < 4u);
+  *w_out = W;
+  int32_t r = static_cast<int32_t>(W >> 30) + zp_out;  // |V| < 2^20 unless big
+  r = r < 0 ? 0 : r;
+  r = r > qmax ? qmax : r;
+  return big ? (T < 0 ? 0 : qmax) : r;
+}
+
+// Exact code for an element flagged by requant_fast96s, from its W: floor(z*) = floor(V) + zp with
+// floor(V) = floor(V + 1/2) - [frac(V + 1/2) < 1/2].
+QHTP_HD int32_t requant_tie_w(int64_t T, int64_t W, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
+                              int32_t zp_out, int32_t qmax) {
+  const uint32_t win = static_cast<uint32_t>(W) & 0x3FFFFFFFu;
+  const int64_t fl = (W >> 30) - (win < (1u << 29) ? 1 : 0) + zp_out;
+  int64_t r = exact_round_near_tie(T, mul, mA, e2, mO, eO, zp_out, fl);
+  r = r < 0 ? 0 : r;
+  r = r > qmax ? qmax : r;
+  return static_cast<int32_t>(r);
+}
+
 // Exact code for an element flagged by requant_fast96; floor_v = floor(z*) from the fast path.
 QHTP_HD int32_t requant_tie(int64_t T, int64_t floor_v, uint32_t mul, int e2, uint64_t mA, uint64_t mO, int eO,
                             int32_t zp_out, int32_t qmax) {
