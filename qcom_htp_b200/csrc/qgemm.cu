@@ -121,6 +121,11 @@ __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// TMEM is released in two halves (activation-hi accumulators, then lo) when the activation has two
+// byte planes and the planes' MMAs are separate instructions.
+template <int PA, int MODE>
+constexpr bool kSplitRelease = PA == 2 && MODE != kModeW16;
+
 template <int PA, int MODE>
 struct GemmCfg {
   static constexpr int kBRows = MODE == kModeExact ? 128 : 256;
@@ -151,8 +156,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 1);
+  uint64_t* tempty = tfull + 1;      // [2]: TMEM half A / half B handed back by the epilogue
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -164,7 +169,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, kEpiWarps);
+    mbar_init(&tempty[0], kEpiWarps);
+    mbar_init(&tempty[1], kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -210,10 +216,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t it = 0, tc = 0;
       bool ok = true;
+      // One K block's MMAs on stage s: the activation-hi plane (TMEM half A) and/or the lo plane
+      // (half B; A16 only).
+      auto issue_kb = [&](uint32_t st_addr, int kb, bool do_hi, bool do_lo) {
+        const uint64_t dA0 = desc_kmajor_sw128(st_addr);
+        const uint64_t dA1 = desc_kmajor_sw128(st_addr + (PA > 1 ? Cfg::kStageA : 0));
+        const uint64_t dB = desc_kmajor_sw128(st_addr + PA * Cfg::kStageA);
+#pragma unroll
+        for (int kk = 0; kk < kTileK / 32; ++kk) {
+          const uint32_t acc = (kb | kk) ? 1u : 0u;
+          const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
+          if constexpr (MODE == kModeW16) {
+            constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);  // u8 act x s8 hi-byte weight
+            constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);  // u8 act x u8 lo-byte weight
+            const uint64_t dBhi = dB + ko;
+            const uint64_t dBlo = dB + ko + (128 * kTileK >> 4);
+            mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
+            mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
+            mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
+            mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
+          } else {
+            constexpr int N = Cfg::kBRows;  // 256 = [q | e'] (f32 mode), 128 = q (exact mode)
+            constexpr uint32_t id = idesc_i8(128, N, 0, 1);
+            if (do_hi) mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
+            if constexpr (PA == 2) {
+              if (do_lo) mma_i8(tmem + N, dA1 + ko, dB + ko, id, acc);
+            }
+          }
+        }
+      };
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++tc) {
-        if (!mbar_wait(tempty, (tc & 1) ^ 1, p.err, kErrTimeoutOther)) break;
+        if (!mbar_wait(&tempty[0], (tc & 1) ^ 1, p.err, kErrTimeoutOther)) break;
         tc_fence_after();
-        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+        int kb = 0;
+        if constexpr (kSplitRelease<PA, MODE>) {
+          // Half A is free: run the hi-plane MMAs of every stage already loaded while the epilogue
+          // still drains half B, then the lo-plane MMAs of those stages.
+          const int D = p.kblocks < S ? p.kblocks : S;
+          for (int d = 0; d < D; ++d) {
+            const int s = (it + d) % S;
+            if (!mbar_wait(&full[s], ((it + d) / S) & 1, p.err, kErrTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_kb(smem_u32(stages + s * Cfg::kStage), d, true, false);
+          }
+          if (!ok) break;
+          if (!mbar_wait(&tempty[1], (tc & 1) ^ 1, p.err, kErrTimeoutOther)) break;
+          tc_fence_after();
+          for (int d = 0; d < D; ++d) {
+            const int s = (it + d) % S;
+            issue_kb(smem_u32(stages + s * Cfg::kStage), d, false, true);
+            mma_commit(&empty[s]);  // stage free once these MMAs have read it
+          }
+          kb = D;
+          it += D;
+        } else {
+          if (!mbar_wait(&tempty[1], (tc & 1) ^ 1, p.err, kErrTimeoutOther)) break;
+          tc_fence_after();
+        }
+        for (; kb < p.kblocks; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full[s], ph, p.err, kErrTimeoutFull)) {
@@ -221,30 +284,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(stages + s * Cfg::kStage);
-          const uint64_t dA0 = desc_kmajor_sw128(st);
-          const uint64_t dA1 = desc_kmajor_sw128(st + (PA > 1 ? Cfg::kStageA : 0));
-          const uint64_t dB = desc_kmajor_sw128(st + PA * Cfg::kStageA);
-#pragma unroll
-          for (int kk = 0; kk < kTileK / 32; ++kk) {
-            const uint32_t acc = (kb | kk) ? 1u : 0u;
-            const uint64_t ko = static_cast<uint64_t>(kk * 2);  // 32 bytes, in 16-byte units
-            if constexpr (MODE == kModeW16) {
-              constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);  // u8 act x s8 hi-byte weight
-              constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);  // u8 act x u8 lo-byte weight
-              const uint64_t dBhi = dB + ko;
-              const uint64_t dBlo = dB + ko + (128 * kTileK >> 4);
-              mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
-              mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
-              mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
-              mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
-            } else {
-              constexpr int N = Cfg::kBRows;  // 256 = [q | e'] (f32 mode), 128 = q (exact mode)
-              constexpr uint32_t id = idesc_i8(128, N, 0, 1);
-              mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
-              if constexpr (PA == 2) mma_i8(tmem + N, dA1 + ko, dB + ko, id, acc);
-            }
-          }
+          issue_kb(smem_u32(stages + s * Cfg::kStage), kb, true, true);
           mma_commit(&empty[s]);  // stage free once these MMAs have read it
         }
         if (ok) mma_commit(tfull);  // accumulators of this tile complete
@@ -266,53 +306,87 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum)) break;
       tc_fence_after();
       const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
-      // ---- drain: TMEM -> int64 accumulators in registers (64 channels of this thread's row)
+      // ---- drain: TMEM -> int64 accumulators in registers (64 channels of this thread's row).  The
+      // effective bias joins T in the requant phase (its record load is already there).
       int64_t T[64];
-#pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 8) {
-        uint32_t s0[8], s1[8], s2[8], s3[8];
+      if constexpr (kSplitRelease<PA, MODE>) {
+        // half A (activation-hi accumulators) in one TMEM wait, handed back at once; then half B,
+        // combined in place into T while the MMA warp already runs the next tile's hi-plane MMAs
+        constexpr int N = Cfg::kBRows;
+        uint32_t sq0[32], sq1[32], se0[32], se1[32];
+        tmem_ld32(tl + 0, sq0);
+        tmem_ld32(tl + 32, sq1);
         if constexpr (MODE == kModeF32) {
-          tmem_ld8(tl + c0, s0);             // sum x(_hi) * q
-          tmem_ld8(tl + 128 + c0, s1);       // sum x(_hi) * e'
-          if constexpr (PA == 2) {
-            tmem_ld8(tl + 256 + c0, s2);     // sum x_lo * q
-            tmem_ld8(tl + 384 + c0, s3);     // sum x_lo * e'
-          }
-        } else if constexpr (MODE == kModeExact) {
-          tmem_ld8(tl + c0, s0);
-          if constexpr (PA == 2) tmem_ld8(tl + 128 + c0, s2);
-        } else {
-          tmem_ld8(tl + c0, s0);             // hi x hi
-          tmem_ld8(tl + 128 + c0, s1);       // hi x lo + lo x hi
-          tmem_ld8(tl + 256 + c0, s2);       // lo x lo
+          tmem_ld32(tl + 128, se0);
+          tmem_ld32(tl + 160, se1);
         }
         tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[0]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t beff = __ldg(&rec[c0 + j].beff);
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          int32_t mqv[16];
           if constexpr (MODE == kModeF32) {
-            const int64_t mq = __ldg(&rec[c0 + j].m_q);
-            int64_t pq = static_cast<int32_t>(s0[j]);
-            int64_t pe = static_cast<int32_t>(s1[j]);
-            if constexpr (PA == 2) {
-              pq = pq * 256 + static_cast<int32_t>(s2[j]);
-              pe = pe * 256 + static_cast<int32_t>(s3[j]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) mqv[j] = __ldg(&rec[c0 + j].m_q);  // in flight with the TMEM loads
+          }
+          uint32_t lq[16], le[16];
+          tmem_ld16(tl + N + c0, lq);                                    // sum x_lo * q
+          if constexpr (MODE == kModeF32) tmem_ld16(tl + N + 128 + c0, le);  // sum x_lo * e'
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t hq = c0 < 32 ? sq0[c0 + j] : sq1[c0 - 32 + j];
+            const int64_t pq = static_cast<int64_t>(static_cast<int32_t>(hq)) * 256 + static_cast<int32_t>(lq[j]);
+            if constexpr (MODE == kModeF32) {
+              const uint32_t he = c0 < 32 ? se0[c0 + j] : se1[c0 - 32 + j];
+              const int64_t pe = static_cast<int64_t>(static_cast<int32_t>(he)) * 256 + static_cast<int32_t>(le[j]);
+              T[c0 + j] = static_cast<int64_t>(mqv[j]) * pq + pe;
+            } else {
+              T[c0 + j] = pq;
             }
-            T[c0 + j] = mq * pq + pe + beff;
-          } else if constexpr (MODE == kModeExact) {
-            int64_t pq = static_cast<int32_t>(s0[j]);
-            if constexpr (PA == 2) pq = pq * 256 + static_cast<int32_t>(s2[j]);
-            T[c0 + j] = pq + beff;
-          } else {
-            T[c0 + j] = static_cast<int64_t>(static_cast<int32_t>(s0[j])) * 65536 +
-                        static_cast<int64_t>(static_cast<int32_t>(s1[j])) * 256 + static_cast<int32_t>(s2[j]) + beff;
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[1]);
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 8) {
+          uint32_t s0[8], s1[8], s2[8];
+          if constexpr (MODE == kModeF32) {
+            tmem_ld8(tl + c0, s0);             // sum x * q
+            tmem_ld8(tl + 128 + c0, s1);       // sum x * e'
+          } else if constexpr (MODE == kModeExact) {
+            tmem_ld8(tl + c0, s0);
+          } else {
+            tmem_ld8(tl + c0, s0);             // hi x hi
+            tmem_ld8(tl + 128 + c0, s1);       // hi x lo + lo x hi
+            tmem_ld8(tl + 256 + c0, s2);       // lo x lo
+          }
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if constexpr (MODE == kModeF32) {
+              const int64_t mq = __ldg(&rec[c0 + j].m_q);
+              T[c0 + j] = mq * static_cast<int32_t>(s0[j]) + static_cast<int32_t>(s1[j]);
+            } else if constexpr (MODE == kModeExact) {
+              T[c0 + j] = static_cast<int32_t>(s0[j]);
+            } else {
+              T[c0 + j] = static_cast<int64_t>(static_cast<int32_t>(s0[j])) * 65536 +
+                          static_cast<int64_t>(static_cast<int32_t>(s1[j])) * 256 + static_cast<int32_t>(s2[j]);
+            }
+          }
+        }
+        // accumulators are in registers: hand TMEM back to the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty[0]);
+          mbar_arrive(&tempty[1]);
+        }
       }
-      // accumulators are in registers: hand TMEM back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty);
       // ---- requant + store, 16 channels per iteration; the register array rotates by 16 so the
       // loop body is emitted once (small instruction footprint)
       const bool row_ok = m < p.M;
@@ -328,6 +402,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint4 rb = __ldg(reinterpret_cast<const uint4*>(rec + c0 + j));       // beff | cmn
             const int tn = __ldg(reinterpret_cast<const int*>(rec + c0 + j) + 6);
             const uint64_t cmn = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
+            T[j] += static_cast<int64_t>((static_cast<uint64_t>(rb.y) << 32) | rb.x);  // + effective bias
             bool nr;
             code[j] = static_cast<uint32_t>(requant_fast96s(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
             near_mask |= nr ? (1u << j) : 0u;
