@@ -373,7 +373,8 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     if args.allgather and world > 1:
         import torch.distributed as dist
         gathered = torch.empty((world, m, n), dtype=torch.uint16, device=dev)
-        ag = lambda: dist.all_gather_into_tensor(gathered.view(torch.int16), out.view(torch.int16))
+        # moved as bytes: NCCL has no 16-bit integer type, and a gather does no arithmetic
+        ag = lambda: dist.all_gather_into_tensor(gathered.view(torch.uint8), out.view(torch.uint8))
         t_ag = max_over_ranks(statistics.mean(timed_steps(ag, max(3, args.steps // 2), 2, flush, world, stream)),
                               world)
         res["allgather"] = {"ms": t_ag * 1e3, "bytes": world * m * n * 2,
