@@ -79,7 +79,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ------------------------------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled loads into the issuing CTA's own shared memory)
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
