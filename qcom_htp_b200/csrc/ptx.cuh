@@ -231,6 +231,13 @@ __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bu
 // Every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start
+// while the previous kernel of the stream still runs; griddep_wait() blocks the calling thread until
+// that kernel has completed and its memory is visible (a no-op for a normally launched kernel).
+// griddep_launch_dependents() lets the next kernel start launching before this one completes.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -192,8 +192,22 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmX);
       tma_prefetch_desc(&tmW);
-      int i = 0;
-      for (int kb = kb0; kb < kb1; ++kb, ++i) {
+      // The weight planes of the first stages load before the activation is awaited (the u16 plane
+      // split runs just before, launched with programmatic dependent launch; a no-op wait otherwise).
+      const int D = (kb1 - kb0) < S ? (kb1 - kb0) : S;
+      for (int d = 0; d < D; ++d) {
+        mbar_arrive_expect_tx(&full[d], Cfg::kStage);
+        tma_load_2d(smem + d * Cfg::kStage, &tmW, &full[d], 0, (tile * p.kblocks + kb0 + d) * Cfg::kWRows);
+      }
+      griddep_wait();
+      for (int d = 0; d < D; ++d) {
+#pragma unroll
+        for (int pl = 0; pl < PA; ++pl)
+          tma_load_2d(smem + d * Cfg::kStage + Cfg::kStageW + pl * Cfg::kStageX, &tmX, &full[d], (kb0 + d) * kTileK,
+                      pl * p.M);
+      }
+      int i = D;
+      for (int kb = kb0 + D; kb < kb1; ++kb, ++i) {
         const int s = i % S;
         if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&full[s], Cfg::kStage);
@@ -417,13 +431,15 @@ cudaError_t launch_dec(const CUtensorMap& tx, const CUtensorMap& tw, DecodeParam
   cfg.blockDim = dim3(kDecThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(prm.splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PA == 2 ? 2 : 1;  // dependent launch only behind this library's own plane split
   return cudaLaunchKernelEx(&cfg, qdecode_kernel<MODE, PA, MP>, tx, tw, prm);
 }
 

@@ -192,10 +192,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tma_prefetch_desc(&tmB);
       uint32_t it = 0;
       bool ok = true;
+      // First tile: the weight planes of the first stages load before the activation is awaited,
+      // overlapping the activation producer (the u16 plane split, launched just before with
+      // programmatic dependent launch); a no-op wait otherwise.
+      const int D = p.kblocks < S ? p.kblocks : S;
+      if (static_cast<int>(blockIdx.x) < total_tiles) {
+        const int m0 = (blockIdx.x % p.m_tiles) * kTileM;
+        const int nt = blockIdx.x / p.m_tiles;
+        for (int d = 0; d < D; ++d) {
+          mbar_arrive_expect_tx(&full[d], Cfg::kStage);
+          tma_load_2d(stages + d * Cfg::kStage + PA * Cfg::kStageA, &tmB, &full[d], 0, (nt * p.kblocks + d) * Cfg::kBRows);
+        }
+        griddep_wait();
+        for (int d = 0; d < D; ++d) {
+#pragma unroll
+          for (int pl = 0; pl < PA; ++pl)
+            tma_load_2d(stages + d * Cfg::kStage + pl * Cfg::kStageA, &tmA, &full[d], d * kTileK,
+                        pl * p.a_plane_rows + m0);
+        }
+        it = static_cast<uint32_t>(D);
+      }
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile % p.m_tiles) * kTileM;
         const int nt = tile / p.m_tiles;
-        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+        for (int kb = (tile == static_cast<int>(blockIdx.x) ? D : 0); kb < p.kblocks; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeoutEmpty)) {
@@ -457,6 +477,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // u16 activation [M,K] -> byte planes hi [M,K] and lo [M,K] (u8), the A operands of the A16 GEMM.
 __global__ void split_u16_planes(const uint16_t* __restrict__ act, uint8_t* __restrict__ hi,
                                  uint8_t* __restrict__ lo, size_t n8) {
+  griddep_launch_dependents();  // the GEMM may start its prologue and weight loads now
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const uint4 v = reinterpret_cast<const uint4*>(act)[i];
@@ -491,8 +512,17 @@ static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, co
   }
   const int total = prm.m_tiles * prm.n_tiles;
   const int grid = total < sm_count() ? total : sm_count();
-  qgemm_kernel<PA, MODE><<<grid, kGemmThreads, Cfg::kSmem, g.stream>>>(ta, tb, prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = g.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = PA == 2 ? 1 : 0;  // only behind this library's own plane split
+  return cudaLaunchKernelEx(&cfg, qgemm_kernel<PA, MODE>, ta, tb, prm);
 }
 
 cudaError_t launch_gemm(const GemmLaunch& g) {
