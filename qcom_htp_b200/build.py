@@ -16,8 +16,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libqhtp.so"
-SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "noalloc.cu"]
-HEADERS = ["ptx.cuh", "requant.cuh", "internal.h"]
+SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "gdn256x2.cu", "noalloc.cu"]
+HEADERS = ["ptx.cuh", "requant.cuh", "internal.h", "gdn_common.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

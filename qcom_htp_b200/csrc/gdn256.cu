@@ -1,6 +1,5 @@
 // GDN / KDA chunk triangular inverse for C = 256 on B200:  T = (I - A)^-1 per chunk, A strictly
-// lower triangular; bf16 in / f32 out, or the u16 code carrier of GdnSolve / gdnbm_solve (value =
-// (code - zp) * scale, example/gdn_native/solve_op/src/GdnSolveOp.cpp:195-281, gdnbm.idl:10-12).
+// lower triangular, bf16 in / f32 out (the u16 code carrier runs the same algorithm in gdn256x2.cu).
 //
 // Same algorithm family as the reference's block solvers (example/gdn_native/solve_op/
 // gdn_solve_ref.c:19-69 forward substitution + block merge; solve_br_op block recursion): the
@@ -34,6 +33,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "gdn_common.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -41,11 +41,9 @@ namespace qhtp {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kC = 256;
+using namespace gdn;
 
 // Shared memory map (bytes from the 1024-aligned base).
-constexpr uint32_t KB = 1024;
 constexpr uint32_t kAULBytes = 32 * KB;  // one diagonal-tile buffer: AU (16K) | AL (16K); two of them
 constexpr uint32_t kAU = 0;              //   AU[q] (q=0..3, 4K each): A[64q + r][64q + c], r < 32
 constexpr uint32_t kAL = 16 * KB;        //   AL[q]: A[64q + 32 + r][64q + c]; rows of the four q stack to M=128
@@ -61,152 +59,9 @@ constexpr uint32_t kZero = 160 * KB;     // 32x32 zero tile of the output type (
 constexpr uint32_t kBar = 164 * KB;
 constexpr uint32_t kSmemBytes = kBar + 64 + 1024;  // barriers + alignment slack
 
-constexpr uint32_t kTile = 4 * KB;  // one 32-row x 128-byte image or staging tile
-
 __device__ __forceinline__ uint32_t rs_off(int q) {
   return q == 0 ? kRS0 : (q == 1 ? kRS1 : (q == 2 ? kRS2 : kRS3));
 }
-
-// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled image.
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return static_cast<uint32_t>(r * 128 + (((c ^ r) & 7) << 4));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&p);
-}
-
-// 32 consecutive f32 values (TMEM columns) of row r -> bf16 chunks c0..c0+3 of an image.
-__device__ __forceinline__ void put_row_bf16(uint8_t* img, int r, int c0, const uint32_t (&v)[32]) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint4 w = make_uint4(pack_bf16(__uint_as_float(v[8 * c + 0]), __uint_as_float(v[8 * c + 1])),
-                               pack_bf16(__uint_as_float(v[8 * c + 2]), __uint_as_float(v[8 * c + 3])),
-                               pack_bf16(__uint_as_float(v[8 * c + 4]), __uint_as_float(v[8 * c + 5])),
-                               pack_bf16(__uint_as_float(v[8 * c + 6]), __uint_as_float(v[8 * c + 7])));
-    *reinterpret_cast<uint4*>(img + swz(r, c0 + c)) = w;
-  }
-}
-
-struct OutCodes {   // u16 output carrier: code = clip(rint(t / sT) + zpT, 0, 65535)
-  float inv_sT, zpT;
-};
-
-__device__ __forceinline__ uint32_t to_code(float t, const OutCodes& oc) {
-  const float q = fminf(fmaxf(rintf(t * oc.inv_sT) + oc.zpT, 0.0f), 65535.0f);
-  return static_cast<uint32_t>(q);
-}
-
-// 32 consecutive f32 values of row r -> a 32x32 staging tile of the output type, in the swizzle of
-// the T tensor map: f32 rows of 128 bytes with the 128-byte swizzle, or u16 code rows of 64 bytes
-// with the 64-byte swizzle (16-byte chunk c at ((c ^ (r >> 1)) & 3) * 16).
-template <bool U16>
-__device__ __forceinline__ void put_row_out(uint8_t* tile, int r, const uint32_t (&v)[32], const OutCodes& oc) {
-  if constexpr (U16) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        w[i] = to_code(__uint_as_float(v[8 * c + 2 * i]), oc) | (to_code(__uint_as_float(v[8 * c + 2 * i + 1]), oc) << 16);
-      *reinterpret_cast<uint4*>(tile + r * 64 + (((c ^ (r >> 1)) & 3) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-  }
-}
-
-// Input element pair -> f32: bf16 bits, or u16 codes (value = (code - zpA) * sA).
-struct InCodes {
-  float sA;
-  int zpA;  // value = (code - zpA) * sA: exact integer difference, one rounding
-};
-
-template <bool U16>
-__device__ __forceinline__ float in_lo(uint32_t w, const InCodes& ic) {
-  if constexpr (U16) return static_cast<float>(static_cast<int>(w & 0xFFFFu) - ic.zpA) * ic.sA;
-  return __uint_as_float(w << 16);
-}
-template <bool U16>
-__device__ __forceinline__ float in_hi(uint32_t w, const InCodes& ic) {
-  if constexpr (U16) return static_cast<float>(static_cast<int>(w >> 16) - ic.zpA) * ic.sA;
-  return __uint_as_float(w & 0xFFFF0000u);
-}
-
-// u16 codes -> bf16 values in place, 16 bytes (8 elements) at a time.
-__device__ __forceinline__ void codes_to_bf16(uint8_t* p, const InCodes& ic) {
-  uint4 raw = *reinterpret_cast<const uint4*>(p);
-  uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = pack_bf16(in_lo<true>(w[i], ic), in_hi<true>(w[i], ic));
-  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// Level 0: forward substitution on one 32x32 diagonal block held in a swizzled bf16 tile (rows 0..31,
-// columns chunk_off*8 .. chunk_off*8+31).  Lane j computes column j:
-//     t[i] = delta(i, j) + sum_{k<i} A[i][k] * t[k]
-// with two partial sums (even / odd k) to halve the dependency chain.  Entries with k >= i are
-// never read.  t[i] is exactly 0 for i < j and exactly 1 for i == j.
-template <bool U16>
-__device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off, int lane, float (&t)[32],
-                                             const InCodes& ic) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float s0 = (i == lane) ? 1.0f : 0.0f, s1 = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      if (8 * c < i) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(tile + swz(i, c + chunk_off));
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int k = 8 * c + e;
-          if (k < i) {
-            const float a = (e & 1) ? in_hi<U16>(w[e >> 1], ic) : in_lo<U16>(w[e >> 1], ic);
-            if (e & 1)
-              s1 = fmaf(a, t[k], s1);
-            else
-              s0 = fmaf(a, t[k], s0);
-          }
-        }
-      }
-    }
-    t[i] = s0 + s1;
-  }
-}
-
-// 16 K steps of one M=128 bf16 MMA group: A K-major at a_addr(s), B MN-major at b_addr(s).
-__device__ __forceinline__ void mma_k16(uint32_t d, uint32_t a, uint32_t b, uint32_t lbo, uint32_t idesc,
-                                        uint32_t acc) {
-  mma_bf16(d, desc_kmajor_sw128(a), desc_mnmajor_sw128(b, lbo), idesc, acc);
-}
-
-// Upper-triangle zero box e (0..27) of a chunk: (column, row) of its top-left corner.
-__device__ __forceinline__ void zero_box(int e, int& x, int& y) {
-  if (e < 4) {  // level 1: rows 64q..64q+31, columns 64q+32..64q+63
-    x = 64 * e + 32;
-    y = 64 * e;
-  } else if (e < 12) {  // level 2: rows 128h..128h+63, columns 128h+64..128h+127
-    const int f = e - 4, h = f >> 2, a = (f >> 1) & 1, b = f & 1;
-    x = 128 * h + 64 + 32 * b;
-    y = 128 * h + 32 * a;
-  } else {  // level 3: rows 0..127, columns 128..255
-    const int f = e - 12;
-    x = 128 + 32 * (f & 3);
-    y = 32 * (f >> 2);
-  }
-}
-
-struct Gdn256Args {
-  void* T;
-  InCodes ic;
-  OutCodes oc;
-  int64_t n_chunks;
-  int* err;
-};
 
 template <bool U16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -638,9 +493,5 @@ cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaSt
   return launch_gdn256<false>(A, T, n_chunks, InCodes{1.0f, 0}, OutCodes{1.0f, 0.0f}, stream);
 }
 
-cudaError_t launch_gdn256_u16(const uint16_t* A, int64_t n_chunks, int zpA, float sA, int zpT, float sT, uint16_t* T,
-                              cudaStream_t stream) {
-  return launch_gdn256<true>(A, T, n_chunks, InCodes{sA, zpA}, OutCodes{1.0f / sT, static_cast<float>(zpT)}, stream);
-}
 
 }  // namespace qhtp
