@@ -86,12 +86,6 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t ran
 }
 // Plain (non-volatile) load from distributed shared memory: ordering against the partial-sum stores
 // comes from the cluster barrier, so independent loads may be scheduled together.
-__device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
-  int32_t v;
-  asm("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
 __device__ __forceinline__ int4 ld_cluster_v4(uint32_t addr) {
   int4 v;
   asm("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -268,6 +262,22 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int quad = warp & 3;
   const int ch_local = quad * 32 + lane;                       // TMEM lane = channel in the tile
   const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  // The channel constants load while the MMAs run (the epilogue warps are idle until then): channel
+  // ch_local without a K split, channels c4..c4+3 (the reduce step's layout) with one.
+  const int c4 = 4 * lane;
+  ChanConst cc, cc4[4];
+  bool cok[4];
+  if (splits == 1) {
+    const int n = tile * 128 + ch_local;
+    cc = load_chan<MODE>(p.rec + (is_epi && n < p.N ? n : 0));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = tile * 128 + c4 + i;
+      cok[i] = is_epi && n < p.N;
+      cc4[i] = load_chan<MODE>(p.rec + (cok[i] ? n : 0));
+    }
+  }
   if (is_epi) {
     ok = mbar_wait(tfull, 0, p.err, kErrTimeoutAccum);
     tc_fence_after();
@@ -281,7 +291,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // (one channel per epilogue thread, all activation rows)
     const int n = tile * 128 + ch_local;
     if (is_epi && n < p.N) {
-      const ChanConst cc = load_chan<MODE>(p.rec + n);
 #pragma unroll 1
       for (int t0 = 0; t0 < MP && t0 < p.M; t0 += 16) {
         uint32_t v[NA][16];
@@ -311,15 +320,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // a row issued before they are summed).
     constexpr int RT = Cfg::kRound;
     const int ew = warp - kDecEpiWarp0;           // 0..3 for the epilogue warps
-    const int c4 = 4 * lane;                       // first of this lane's four channels
-    ChanConst cc4[4];
-    bool cok[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int n = tile * 128 + c4 + i;
-      cok[i] = is_epi && n < p.N;
-      cc4[i] = load_chan<MODE>(p.rec + (cok[i] ? n : 0));
-    }
     const uint32_t red_s = smem_u32(red);
     uint32_t peer[8];
 #pragma unroll
