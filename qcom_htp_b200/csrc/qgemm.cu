@@ -134,13 +134,28 @@ struct GemmCfg {
   static constexpr int kStage = PA * kStageA + kStageB;
   static constexpr int kStagesRaw = (200 * 1024) / kStage;
   static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
-  static constexpr int kSmem = kStages * kStage + 1024 + 256;
+  static constexpr int kRecBytes = kTileN * 32;  // the tile's channel records, staged for the epilogue
+  static constexpr int kSmem = kStages * kStage + kRecBytes + 1024 + 256;
 };
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
+}
+
+// Named barrier 1 over the epilogue warps, and the same barrier ANDing a predicate (every thread
+// leaves with the same answer, so a bounded wait that gave up anywhere stops all of them together).
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.cta.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(32 * kEpiWarps)
+      : "memory");
+  return r != 0;
 }
 
 template <int PA, int MODE>
@@ -153,7 +168,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
+  ChannelRecord* rec_s = reinterpret_cast<ChannelRecord*>(smem + S * Cfg::kStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage + Cfg::kRecBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 1;      // [2]: TMEM half A / half B handed back by the epilogue
@@ -322,8 +338,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
       const int m = (tile % p.m_tiles) * kTileM + row;
       const int n0 = (tile / p.m_tiles) * kTileN + half * 64;
-      const ChannelRecord* rec = p.rec + n0;
-      if (!mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum)) break;
+      // The tile's 128 channel records (4 KB) -> shared memory while the accumulators are still being
+      // formed: the drain and the requant read their constants there, not from L2.
+      epi_bar();  // every epilogue warp is done with the previous tile's records
+      {
+        const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..255, 16 bytes each
+        reinterpret_cast<uint4*>(rec_s)[et] =
+            __ldg(reinterpret_cast<const uint4*>(p.rec + (tile / p.m_tiles) * kTileN) + et);
+      }
+      if (!epi_bar_and(mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum))) break;  // also publishes rec_s
+      const ChannelRecord* rec = rec_s + half * 64;
       tc_fence_after();
       const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
       // ---- drain: TMEM -> int64 accumulators in registers (64 channels of this thread's row).  The
@@ -349,7 +373,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           int32_t mqv[16];
           if constexpr (MODE == kModeF32) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) mqv[j] = __ldg(&rec[c0 + j].m_q);  // in flight with the TMEM loads
+            for (int j = 0; j < 16; ++j) mqv[j] = rec[c0 + j].m_q;
           }
           uint32_t lq[16], le[16];
           tmem_ld16(tl + N + c0, lq);                                    // sum x_lo * q
@@ -389,7 +413,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             if constexpr (MODE == kModeF32) {
-              const int64_t mq = __ldg(&rec[c0 + j].m_q);
+              const int64_t mq = rec[c0 + j].m_q;
               T[c0 + j] = mq * static_cast<int32_t>(s0[j]) + static_cast<int32_t>(s1[j]);
             } else if constexpr (MODE == kModeExact) {
               T[c0 + j] = static_cast<int32_t>(s0[j]);
@@ -419,8 +443,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           int64_t fl[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const uint4 rb = __ldg(reinterpret_cast<const uint4*>(rec + c0 + j));       // beff | cmn
-            const int tn = __ldg(reinterpret_cast<const int*>(rec + c0 + j) + 6);
+            const uint4 rb = *reinterpret_cast<const uint4*>(rec + c0 + j);       // beff | cmn
+            const int tn = rec[c0 + j].tn;
             const uint64_t cmn = (static_cast<uint64_t>(rb.w) << 32) | rb.z;
             T[j] += static_cast<int64_t>((static_cast<uint64_t>(rb.y) << 32) | rb.x);  // + effective bias
             bool nr;
@@ -430,7 +454,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (near_mask != 0) {  // rare: within 2^-29 of a tie -> exact decision
             for (int j = 0; j < 16; ++j) {
               if (near_mask & (1u << j)) {
-                const uint32_t wb = __ldg(&rec[c0 + j].wbits);
+                const uint32_t wb = rec[c0 + j].wbits;
                 const uint32_t ms = (wb & 0x7FFFFFu) | 0x800000u;
                 const int es = static_cast<int>((wb >> 23) & 0xFFu) - 150;
                 const uint32_t mul = MODE == kModeF32 ? 1u : ms;
