@@ -157,6 +157,22 @@ QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan *plan, const void *act, uint32_t
 QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
                                    void *stream);
 
+/* qhtp_matmul_run from and to HOST memory: out_host[M,N] from act_host[M,K].  No counterpart in
+ * the reference (its op runs on buffers the QNN runtime has placed); for serving from host memory.
+ * The rows are processed in chunks of chunk_rows (0: the library picks ~8 chunks of a multiple of
+ * 128 rows): chunk i's host->device copy runs on a library stream, its GEMM on `stream`, its
+ * device->host copy on a second library stream, so copies in both directions overlap the GEMMs of
+ * the other chunks.  act_dev [M,K] and out_dev [M,N] are device staging buffers (16-byte aligned);
+ * workspace >= qhtp_matmul_workspace_bytes(plan, chunk_rows) (the error word for qhtp_matmul_check
+ * is the one of an M = chunk_rows call; *chunk_rows_used reports the chunk size if non-NULL).  The
+ * host buffers must be pinned (page-locked) for the copies to be asynchronous.  The whole
+ * operation is ordered after prior work on `stream`, and later work on `stream` after it: the
+ * host output is complete once `stream` is.  Calls no cudaMalloc / cudaFree (the library's two
+ * copy streams and its events are created once per device). */
+QhtpStatus qhtp_matmul_run_host(const QhtpMatmulPlan *plan, const void *act_host, uint32_t m, void *out_host,
+                                void *act_dev, void *out_dev, void *workspace, size_t workspace_bytes,
+                                uint32_t chunk_rows, uint32_t *chunk_rows_used, void *stream);
+
 /* Synchronize `stream` and read the device error word of `workspace`; clears it.  Returns
  * QHTP_STATUS_RUNTIME_ERROR if a kernel recorded an error (code in *device_code if non-NULL). */
 QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan *plan, void *workspace, uint32_t m, int *device_code,

@@ -75,6 +75,9 @@ SIGNATURES = {
                                   C.c_size_t, C.c_void_p]),
     "qhtp_matmul_run_noalloc": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p,
                                           C.c_void_p]),
+    "qhtp_matmul_run_host": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_void_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_uint32),
+                                       C.c_void_p]),
     "qhtp_matmul_check": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.POINTER(C.c_int),
                                     C.c_void_p]),
     "qhtp_matmul_read_records": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_size_t, C.c_void_p]),

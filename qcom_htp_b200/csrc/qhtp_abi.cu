@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "internal.h"
 #include "requant.cuh"
@@ -70,6 +71,50 @@ void set_last_message(const char* msg) { g_last_message = msg; }
 
 namespace {
 QhtpStatus from_cuda(cudaError_t e) { return qhtp::status_from_cuda(e); }
+
+// qhtp_matmul_run_host: per device, two copy streams (host->device, device->host) and the events
+// that chain each row chunk's copy in, GEMM and copy out.  Created on first use, kept until the
+// process exits; one call at a time uses them (the events are re-recorded by every call).
+constexpr uint32_t kHostMaxChunks = 64;
+constexpr int kHostMaxDevices = 64;
+struct HostPipe {
+  std::mutex mu;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  cudaEvent_t copied[kHostMaxChunks] = {}, computed[kHostMaxChunks] = {};
+};
+
+HostPipe* host_pipe() {
+  static std::mutex init_mu;
+  static HostPipe* pipes[kHostMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kHostMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(init_mu);
+  if (pipes[dev] == nullptr) {
+    HostPipe* hp = new HostPipe();
+    bool ok = cudaStreamCreateWithFlags(&hp->in, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&hp->out, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&hp->start, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&hp->done, cudaEventDisableTiming) == cudaSuccess;
+    for (uint32_t i = 0; ok && i < kHostMaxChunks; ++i)
+      ok = cudaEventCreateWithFlags(&hp->copied[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&hp->computed[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) return nullptr;  // what was created stays with the process
+    pipes[dev] = hp;
+  }
+  return pipes[dev];
+}
+
+// Rows per chunk: the caller's choice, or ~8 chunks of a multiple of 128 rows (the GEMM's row
+// tile); never more than kHostMaxChunks chunks, never more than M rows.
+uint32_t host_chunk_rows(uint32_t m, uint32_t req) {
+  uint32_t r = req;
+  if (r == 0) r = ((m + 7) / 8 + 127) / 128 * 128;
+  const uint32_t min_r = (m + kHostMaxChunks - 1) / kHostMaxChunks;
+  if (r < min_r) r = min_r;
+  if (r > m) r = m;
+  return r;
+}
 }  // namespace
 
 extern "C" {
@@ -208,6 +253,64 @@ QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan* plan, const void* act, uint32_t
   g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, m));
   g.stream = as_stream(stream);
   return from_cuda(launch_gemm(g));
+}
+
+QhtpStatus qhtp_matmul_run_host(const QhtpMatmulPlan* plan, const void* act_host, uint32_t m, void* out_host,
+                                void* act_dev, void* out_dev, void* workspace, size_t workspace_bytes,
+                                uint32_t chunk_rows, uint32_t* chunk_rows_used, void* stream) {
+  if (!plan_ok(plan) || plan->prepared == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (act_host == nullptr || out_host == nullptr || act_dev == nullptr || out_dev == nullptr || workspace == nullptr ||
+      m == 0)
+    return QHTP_STATUS_INVALID_ARGUMENT;
+  if (!aligned(act_dev, 16) || !aligned(out_dev, 16) || !aligned(workspace, 256)) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (m > (1u << 24)) return QHTP_STATUS_UNSUPPORTED;
+  const uint32_t rows = host_chunk_rows(m, chunk_rows);
+  if (workspace_bytes < qhtp_matmul_workspace_bytes(plan, rows)) {
+    set_last_message("qhtp_matmul_run_host: workspace smaller than qhtp_matmul_workspace_bytes(plan, chunk rows)");
+    return QHTP_STATUS_INVALID_ARGUMENT;
+  }
+  if (chunk_rows_used) *chunk_rows_used = rows;
+  HostPipe* hp = host_pipe();
+  if (hp == nullptr) return QHTP_STATUS_RUNTIME_ERROR;
+  std::lock_guard<std::mutex> lock(hp->mu);  // the pipe's streams and events serve one call at a time
+  const size_t act_row = static_cast<size_t>(plan->k) * (plan->act_bits / 8);
+  const size_t out_row = static_cast<size_t>(plan->n) * (plan->out_bits / 8);
+  cudaStream_t s = as_stream(stream);
+  // the copies start after prior work on `stream` (which may still use the staging buffers)
+  cudaError_t e = cudaEventRecord(hp->start, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->in, hp->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->out, hp->start, 0);
+  GemmLaunch g;
+  g.plan = plan;
+  g.planes = static_cast<uint8_t*>(workspace);
+  g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, rows));
+  g.stream = s;
+  const uint32_t chunks = (m + rows - 1) / rows;
+  for (uint32_t c = 0; c < chunks && e == cudaSuccess; ++c) {
+    const uint32_t r0 = c * rows, rc = m - r0 < rows ? m - r0 : rows;
+    uint8_t* a_d = static_cast<uint8_t*>(act_dev) + r0 * act_row;
+    uint8_t* o_d = static_cast<uint8_t*>(out_dev) + r0 * out_row;
+    // chunk c: host -> device (copy stream 1), GEMM (the caller's stream), device -> host (stream 2)
+    e = cudaMemcpyAsync(a_d, static_cast<const uint8_t*>(act_host) + r0 * act_row, rc * act_row,
+                        cudaMemcpyHostToDevice, hp->in);
+    if (e == cudaSuccess) e = cudaEventRecord(hp->copied[c], hp->in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, hp->copied[c], 0);
+    if (e == cudaSuccess) {
+      g.act = a_d;
+      g.m = rc;
+      g.out = o_d;
+      e = launch_gemm(g);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(hp->computed[c], s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->out, hp->computed[c], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + r0 * out_row, o_d, rc * out_row, cudaMemcpyDeviceToHost,
+                          hp->out);
+  }
+  // later work on `stream` follows the last copy back
+  if (e == cudaSuccess) e = cudaEventRecord(hp->done, hp->out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, hp->done, 0);
+  return from_cuda(e);
 }
 
 QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan* plan, void* workspace, uint32_t m, int* device_code,

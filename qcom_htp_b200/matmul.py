@@ -139,11 +139,48 @@ class QuantMatMul:
             C.byref(self.plan), _ptr(act), m, _ptr(out), _ptr(ws), ws.numel(), _stream_handle(stream)))
         return out
 
-    def check_device(self, m: int, stream=None) -> None:
+    def run_host(self, act_host: torch.Tensor, out_host: torch.Tensor | None = None, chunk_rows: int = 0,
+                 stream=None) -> torch.Tensor:
+        """qhtp_matmul_run_host: activation and output in (pinned) host memory; row chunks whose
+        copies in both directions overlap the GEMMs of the other chunks.  The device staging buffers
+        and the workspace are kept per M.  Returns when the work is enqueued: the output is complete
+        once `stream` is (synchronize before reading it)."""
+        if act_host.dim() != 2 or act_host.shape[1] != self.k or act_host.is_cuda:
+            raise ValueError(f"act_host must be a host [M, {self.k}] tensor")
+        if act_host.dtype != _dt(self.act_bits) or not act_host.is_contiguous():
+            raise TypeError(f"act_host must be a contiguous {_dt(self.act_bits)} tensor")
+        m = act_host.shape[0]
+        if out_host is None:
+            out_host = torch.empty((m, self.n), dtype=_dt(self.out_bits)).pin_memory()
+        elif (out_host.shape != (m, self.n) or out_host.dtype != _dt(self.out_bits) or out_host.is_cuda
+              or not out_host.is_contiguous()):
+            raise ValueError("bad host output tensor")
+        key = ("host", m, chunk_rows)
+        st = self._ws.get(key)
+        if st is None:
+            nbytes = int(L.lib.qhtp_matmul_workspace_bytes(C.byref(self.plan), m))  # >= any chunk's
+            st = (torch.empty((m, self.k), dtype=_dt(self.act_bits), device=self.device),
+                  torch.empty((m, self.n), dtype=_dt(self.out_bits), device=self.device),
+                  torch.zeros(nbytes, dtype=torch.uint8, device=self.device))
+            self._ws[key] = st
+        act_d, out_d, ws = st
+        used = C.c_uint32(0)
+        L.check("qhtp_matmul_run_host", L.lib.qhtp_matmul_run_host(
+            C.byref(self.plan), act_host.data_ptr(), m, out_host.data_ptr(), _ptr(act_d), _ptr(out_d), _ptr(ws),
+            ws.numel(), chunk_rows, C.byref(used), _stream_handle(stream)))
+        self.host_chunk_rows = used.value
+        self._host_ws = ws
+        return out_host
+
+    def check_host(self, stream=None) -> None:
+        """check_device for the last run_host call (its workspace, its chunk size)."""
+        self.check_device(self.host_chunk_rows, stream, workspace=self._host_ws)
+
+    def check_device(self, m: int, stream=None, workspace: torch.Tensor | None = None) -> None:
         """Synchronize and raise if a kernel recorded a device-side error for workspace(m)."""
         code = C.c_int(0)
-        st = L.lib.qhtp_matmul_check(C.byref(self.plan), _ptr(self.workspace(m)), m, C.byref(code),
-                                     _stream_handle(stream))
+        ws = self.workspace(m) if workspace is None else workspace
+        st = L.lib.qhtp_matmul_check(C.byref(self.plan), _ptr(ws), m, C.byref(code), _stream_handle(stream))
         if st != L.OK:
             raise L.QhtpError(f"qhtp_matmul_check (device code {code.value})", st)
 

@@ -71,6 +71,8 @@ def test_null_and_unplanned_calls_are_errors(L):
     assert L.lib.qhtp_matmul_plan(None, C.byref(p)) == L.INVALID_ARGUMENT
     assert L.lib.qhtp_matmul_run(C.byref(p), None, 1, None, None, 0, None) == L.INVALID_ARGUMENT
     assert L.lib.qhtp_matmul_prepare(C.byref(p), None, None, 0, None) == L.INVALID_ARGUMENT
+    assert L.lib.qhtp_matmul_run_host(C.byref(p), None, 1, None, None, None, None, 0, 0, None, None) \
+        == L.INVALID_ARGUMENT
     assert L.lib.qhtp_u8i8_run_prepared(None) == L.INVALID_ARGUMENT
     assert L.lib.qhtp_gdn_inverse_bf16(None, None, 1, 256, None) == L.INVALID_ARGUMENT
     assert L.lib.qhtp_gdn_inverse_bf16(1024, 1024, 1, 96, None) == L.UNSUPPORTED
