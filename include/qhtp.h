@@ -187,6 +187,38 @@ QhtpStatus qhtp_matmul_read_records(const QhtpMatmulPlan *plan, void *host_dst, 
 QhtpStatus qhtp_lpbq_expand_i8(const uint8_t *w4_kpair, const uint8_t *block_scale, uint32_t k, uint32_t n,
                                uint32_t block, int8_t *out_nk, void *stream);
 
+/* ---- Reference weight wire formats -> this library's plain weight carriers.
+ * The layouts the reference's QNN MatMul ops read from their ONNX initializers
+ * (example/qnn_hmx_matmul_common/gen_quant_chain.py:285-742), so existing weight files load
+ * unchanged: decode once on the device, then pass the plain carrier to qhtp_matmul_plan/prepare.
+ * Output: int8 [N, K] row-major for the W8 formats; int4 K-pair bytes [K/2, N] (byte (k/2)*N + n,
+ * low nibble = even k, two's complement) for the W4 formats. ---- */
+typedef enum QhtpWireFormat {
+  QHTP_WIRE_W8_RAW_KN = 1,            /* int8 [K, N] (w8a16 "raw"; u8i8 with QHTP_WIRE_XOR80), :728-741 */
+  QHTP_WIRE_W8_KMAJOR_TILE32 = 2,     /* 32x32 K-major HMX tiles, dst = (r/4)*128 + c*4 + r%4, :285-303 */
+  QHTP_WIRE_W8_KMAJOR_SPLIT128 = 3,   /* K-major tiles per 128-channel stream, :306-314 */
+  QHTP_WIRE_W4_TILE32X64_NPAIR32 = 4, /* W4A8 HMX: 32x64 K-major tiles, byte = channels n | n+32, :686-712 */
+  QHTP_WIRE_W4_KPAIR = 5,             /* [K/2, N] K-pairs (also the LPBQ pre-chain weight), :369-382 */
+  QHTP_WIRE_W4_NMAJOR_KPAIR = 6,      /* [N, K/2] K-pairs, :385-398 */
+  QHTP_WIRE_W4_NMAJOR_K4 = 7,         /* N32 tiles, K8 groups, k / k+4 pairs, :401-422 */
+  QHTP_WIRE_W4_KBLOCK32_NMAJOR_K4 = 8,/* K32 blocks, then N32 tiles, k / k+4 pairs, :425-452 */
+  QHTP_WIRE_W4_NPAIR_ADJACENT = 9,    /* [N/2, K], byte = channels 2j | 2j+1, :455-468 */
+  QHTP_WIRE_W4_NPAIR_TILE32 = 10,     /* [N/2, K], byte = channels n | n+32 per 64-channel tile, :471-489 */
+  QHTP_WIRE_W4_FULL_CODES = 11        /* [K, N], one code per byte, :619-627 */
+} QhtpWireFormat;
+#define QHTP_WIRE_XOR80 1u  /* every carrier byte XOR 0x80 (the int8 carriers of the QNN sidecar) */
+#define QHTP_WIRE_HILO 2u   /* "hilo" orders: the first element of a byte pair in the high nibble */
+#define QHTP_WIRE_BIASED 4u /* "biased" nibble encoding: code = v + 8 */
+
+/* Bytes of a wire-format weight [K, N] (0 for an unknown format). */
+size_t qhtp_wire_bytes(uint32_t format, uint32_t k, uint32_t n);
+
+/* Decode `wire` (device, qhtp_wire_bytes) into `plain` (device, K*N bytes for W8 formats, K*N/2
+ * for W4).  QHTP_STATUS_UNSUPPORTED for shapes the layout cannot hold (tile multiples of K / N).
+ * Asynchronous on `stream`. */
+QhtpStatus qhtp_weights_from_wire(uint32_t format, uint32_t flags, const void *wire, size_t wire_bytes, uint32_t k,
+                                  uint32_t n, void *plain, size_t plain_bytes, void *stream);
+
 /* ---- prepared-run entry points, one per family (hm_<family>_run_prepared,
  *      handwritten_hmx_matmul.h:28-50).  chain > 1 re-applies the same op chain times, each
  *      output feeding the next activation (requires K == N and equal act/out widths); the

@@ -78,6 +78,9 @@ SIGNATURES = {
     "qhtp_matmul_run_host": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_uint32),
                                        C.c_void_p]),
+    "qhtp_wire_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32]),
+    "qhtp_weights_from_wire": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint32,
+                                         C.c_void_p, C.c_size_t, C.c_void_p]),
     "qhtp_matmul_check": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.POINTER(C.c_int),
                                     C.c_void_p]),
     "qhtp_matmul_read_records": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_size_t, C.c_void_p]),
@@ -130,3 +133,10 @@ def status_string(status: int) -> str:
 def check(fn: str, status: int) -> None:
     if status != OK:
         raise QhtpError(fn, status)
+
+
+# qhtp_weights_from_wire layouts and flags (QhtpWireFormat, QHTP_WIRE_* in include/qhtp.h)
+WIRE_FORMAT = {"w8_raw_kn": 1, "w8_kmajor_tile32": 2, "w8_kmajor_split128": 3, "w4_tile32x64_npair32": 4,
+               "w4_kpair": 5, "w4_nmajor_kpair": 6, "w4_nmajor_k4": 7, "w4_kblock32_nmajor_k4": 8,
+               "w4_npair_adjacent": 9, "w4_npair_tile32": 10, "w4_full_codes": 11}
+WIRE_XOR80, WIRE_HILO, WIRE_BIASED = 1, 2, 4

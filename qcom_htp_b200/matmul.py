@@ -252,3 +252,20 @@ def requant_code_host(T: int, cm: int, cshift: int, mul: int, e2: int, act_mant:
                       out_exp2: int, zp_out: int, qmax: int) -> int:
     """The kernels' exact requant decision, evaluated on the host (testing aid)."""
     return int(L.lib.qhtp_requant_code_host(T, cm, cshift, mul, e2, act_mant, out_mant, out_exp2, zp_out, qmax))
+
+
+def weights_from_wire(fmt: str | int, wire: torch.Tensor, k: int, n: int, *, xor80: bool = False, hilo: bool = False,
+                      biased: bool = False, stream=None) -> torch.Tensor:
+    """Decode a weight in one of the reference's wire layouts (its QNN initializer bytes, on the
+    device) into this library's plain carrier: int8 [N, K] for the W8 layouts, the int4 K-pair bytes
+    [K/2, N] (uint8) for the W4 layouts.  ``fmt``: a key of ``_lib.WIRE_FORMAT`` or its id."""
+    f = L.WIRE_FORMAT[fmt] if isinstance(fmt, str) else int(fmt)
+    flags = (L.WIRE_XOR80 if xor80 else 0) | (L.WIRE_HILO if hilo else 0) | (L.WIRE_BIASED if biased else 0)
+    if not wire.is_cuda or not wire.is_contiguous():
+        raise TypeError("wire must be a contiguous CUDA tensor")
+    w8 = f <= L.WIRE_FORMAT["w8_kmajor_split128"]
+    out = torch.empty((n, k) if w8 else (k // 2, n), dtype=torch.int8 if w8 else torch.uint8, device=wire.device)
+    L.check("qhtp_weights_from_wire", L.lib.qhtp_weights_from_wire(
+        f, flags, _ptr(wire), wire.numel() * wire.element_size(), k, n, _ptr(out), out.numel(),
+        _stream_handle(stream)))
+    return out
