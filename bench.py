@@ -455,6 +455,22 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
                           "ms_per_step": t16 * 1e3, "hbm_gbs": b16 / t16 / 1e9, "hbm_frac": b16 / t16 / 1e9 / pk["hbm_gbs"],
                           "note": "u16 codes A -> u16 codes T (zp 32768), algorithmic bytes 2C^2 + 2C^2 per chunk"}
     del Ac, Tc
+    # the step on the input side fused in: A built on the SM from raw keys, beta and per-token log
+    # gates (gdn_chunk Stage A, scripts/gdn_ref_kernel.py:66-82), then inverted; same chunk count
+    from qcom_htp_b200 import gdn_chunk_inverse
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    kk = torch.randn((n_chunks, C, 128), generator=gen, device=dev).to(torch.bfloat16)
+    bb = torch.sigmoid(torch.randn((n_chunks, C), generator=gen, device=dev))
+    gg = torch.nn.functional.logsigmoid(0.5 * torch.randn((n_chunks, C), generator=gen, device=dev) - 2.0)
+    fnf = lambda: gdn_chunk_inverse(kk, bb, gg, T)
+    tf = max_over_ranks(statistics.mean(timed_steps(fnf, steps, args.warmup, flush, world, stream)), world)
+    bf = n_chunks * (C * 128 * 2 + C * 4 * 2 + C * C * 4)
+    res["fused_A"] = {"metric": "gdn_chunk_inverse_chunks_per_s", "value": n_chunks * world / tf,
+                      "ms_per_step": tf * 1e3, "hbm_gbs": bf / tf / 1e9, "hbm_frac": bf / tf / 1e9 / pk["hbm_gbs"],
+                      "kernel": "gdn256f_kernel (Gram MMAs + A epilogue + the C=256 inverse)",
+                      "note": "k bf16 [C,128], beta and log gates f32 [C] -> T f32: algorithmic bytes 256C + 8C + 4C^2 "
+                              "per chunk; A (bf16 [C,C]) never written or read"}
+    del kk, bb, gg
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_gdn_baseline(A)
     if not secondary:

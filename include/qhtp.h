@@ -259,6 +259,15 @@ QhtpStatus qhtp_w16a16_run_prepared(const QhtpPreparedRun *run);
 /* A bf16 [n_chunks, C, C] -> T float32 [n_chunks, C, C]. */
 QhtpStatus qhtp_gdn_inverse_bf16(const void *A, float *T, int64_t n_chunks, int32_t C, void *stream);
 
+/* The chunk's A built on the GPU from the gated-delta-rule inputs and inverted in the same kernel, as
+ * the reference's chunk kernel does (Stage A of gdn_chunk, scripts/gdn_ref_kernel.py:66-82):
+ * k L2-normalised (eps 1e-6), g = cumsum of the per-token log gates over the chunk,
+ * A[i][j] = -beta_i (k_i . k_j) exp(g_i - g_j) for i > j, T = (I - A)^-1.  A never reaches memory.
+ * k bf16 [n_chunks, C, Dk] (raw keys), beta and g float32 [n_chunks, C] -> T float32 [n_chunks, C, C].
+ * C = 256 and Dk = 128 (QHTP_STATUS_UNSUPPORTED otherwise); 16-byte aligned buffers. */
+QhtpStatus qhtp_gdn_chunk_inverse(const void *k, const float *beta, const float *g, float *T, int64_t n_chunks,
+                                  int32_t C, int32_t dk, void *stream);
+
 /* u16-code carrier (gdnbm.idl:10-12, gdn_solve_oc_check.py:28-29): value = (code - zp) * scale.
  * A codes [n_chunks, C, C] -> T codes, T_code = clip(rint(T / sT) + zpT, 0, 65535). */
 QhtpStatus qhtp_gdn_solve_u16(const uint16_t *A, int64_t n_chunks, int32_t C, int32_t zpA, float sA,

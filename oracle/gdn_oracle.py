@@ -6,6 +6,9 @@
                        This is the chunk-local A of ``scripts/gdn_ref_kernel.py:71-87`` (its l2norm at
                        :31-32, the decay at :79-83; the sign there is folded into A so that
                        T = (I - A)^-1, as in ``solve_op/gdn_solve_ref.c:1``).
+* ``chunk_A_from_kbg``: the same A from the raw gated-delta-rule inputs (k, beta, per-token log
+                       gates), as the reference's fused chunk kernel builds it (Stage A of
+                       ``gdn_chunk``, ``scripts/gdn_ref_kernel.py:66-82``); ``make_kbg`` draws them.
 * ``inverse_fp64``   : the precision oracle, fp64 ``inv(I - A)`` per chunk
                        (``scripts/gdn_solve_oc_check.py:30``), computed by triangular solve.
 * ``oc``             : ``||T - Tref||_F / (||Tref||_F + 1e-12)`` over all chunks jointly
@@ -49,6 +52,35 @@ def make_chunk_A(n_chunks: int, C: int = 256, dk: int = 128, seed: int = 0x6D6E,
     A = -(beta[:, :, None] * kk * decay)
     A = np.where(tril, A, 0.0).astype(np.float32)
     return _bf16_round(A) if as_bf16 else A
+
+
+def chunk_A_from_kbg(k: np.ndarray, beta: np.ndarray, g_tok: np.ndarray) -> np.ndarray:
+    """fp64 strictly-lower A of each chunk from the gated-delta-rule inputs, restating the Stage-A
+    prefix of ``gdn_chunk`` (``scripts/gdn_ref_kernel.py:66-82``): k L2-normalised over Dk (eps 1e-6,
+    :31-32), k_beta = k * beta, g = cumsum of the per-token log gates over the chunk (:72), decay =
+    exp(g_i - g_j) on and below the diagonal, attn = -(k_beta k^T) * decay with the diagonal and the
+    upper triangle zeroed (:75-77).  A = attn, so that T = (I - A)^-1 (the reference's forward
+    substitution and ``+ eye`` at :78-81).  k [n, C, Dk]; beta, g_tok [n, C]."""
+    k = np.asarray(k, np.float64)
+    k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+    kb = k * np.asarray(beta, np.float64)[..., None]
+    g = np.cumsum(np.asarray(g_tok, np.float64), axis=-1)
+    C = k.shape[-2]
+    strict = np.tril(np.ones((C, C), bool), -1)
+    diff = np.where(strict, g[..., :, None] - g[..., None, :], -np.inf)
+    return np.where(strict, -np.einsum("ncd,nkd->nck", kb, k) * np.exp(diff), 0.0)
+
+
+def make_kbg(n_chunks: int, C: int = 256, dk: int = 128, seed: int = 0x6D6F):
+    """Synthetic gated-delta-rule chunk inputs of the BASELINE GDN config: raw k ~ N(0,1) rounded to
+    bf16 [n, C, Dk], beta = sigmoid(N(0,1)) [n, C], per-token log gates logsigmoid(0.5 N(0,1) - 2)
+    [n, C] (f32)."""
+    rng = np.random.default_rng(seed)
+    k = _bf16_round(rng.standard_normal((n_chunks, C, dk)).astype(np.float32))
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((n_chunks, C))))).astype(np.float32)
+    z = 0.5 * rng.standard_normal((n_chunks, C)) - 2.0
+    g_tok = (-np.logaddexp(0.0, -z)).astype(np.float32)
+    return k, beta, g_tok
 
 
 def inverse_fp64(A: np.ndarray) -> np.ndarray:

@@ -93,6 +93,8 @@ SIGNATURES = {
     "qhtp_w4a16_run_prepared": (C.c_int, [C.POINTER(QhtpPreparedRun)]),
     "qhtp_w16a16_run_prepared": (C.c_int, [C.POINTER(QhtpPreparedRun)]),
     "qhtp_gdn_inverse_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
+    "qhtp_gdn_chunk_inverse": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                         C.c_int32, C.c_void_p]),
     "qhtp_gdn_solve_u16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_float, C.c_int32,
                                      C.c_float, C.c_void_p, C.c_void_p]),
     "qhtp_requant_code_host": (C.c_int32, [C.c_int64, C.c_uint64, C.c_int32, C.c_uint32, C.c_int32, C.c_uint64,

@@ -68,6 +68,10 @@ cudaError_t launch_gdn_u16(const uint16_t* A, int64_t n_chunks, int C, int zpA, 
 // gdn256.cu: C = 256, tensor-core doubling kernel (bf16 in / f32 out, or u16 codes in / out)
 bool gdn256_supported(const void* A, const void* T, int64_t n_chunks);
 cudaError_t launch_gdn256_bf16(const void* A, float* T, int64_t n_chunks, cudaStream_t stream);
+// gdn256f.cu: fused A construction (k, beta, log gates) + inverse, C = 256, Dk = 128
+bool gdn256f_supported(const void* k, const float* beta, const float* g, const float* T, int64_t n_chunks);
+cudaError_t launch_gdn256_fused(const void* k, const float* beta, const float* g, float* T, int64_t n_chunks,
+                                cudaStream_t stream);
 cudaError_t launch_gdn256_u16(const uint16_t* A, int64_t n_chunks, int zpA, float sA, int zpT, float sT, uint16_t* T,
                               cudaStream_t stream);
 

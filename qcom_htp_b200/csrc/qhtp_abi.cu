@@ -402,6 +402,15 @@ QhtpStatus qhtp_gdn_inverse_bf16(const void* A, float* T, int64_t n_chunks, int3
   return from_cuda(launch_gdn_bf16(A, T, n_chunks, C, as_stream(stream)));
 }
 
+QhtpStatus qhtp_gdn_chunk_inverse(const void* k, const float* beta, const float* g, float* T, int64_t n_chunks,
+                                  int32_t C, int32_t dk, void* stream) {
+  if (k == nullptr || beta == nullptr || g == nullptr || T == nullptr || n_chunks <= 0)
+    return QHTP_STATUS_INVALID_ARGUMENT;
+  if (C != 256 || dk != 128) return QHTP_STATUS_UNSUPPORTED;
+  if (!gdn256f_supported(k, beta, g, T, n_chunks)) return QHTP_STATUS_INVALID_ARGUMENT;
+  return from_cuda(launch_gdn256_fused(k, beta, g, T, n_chunks, as_stream(stream)));
+}
+
 QhtpStatus qhtp_gdn_solve_u16(const uint16_t* A, int64_t n_chunks, int32_t C, int32_t zpA, float sA, int32_t zpT,
                               float sT, uint16_t* T, void* stream) {
   if (A == nullptr || T == nullptr || n_chunks <= 0) return QHTP_STATUS_INVALID_ARGUMENT;

@@ -38,6 +38,31 @@ def gdn_inverse(A: torch.Tensor, out: torch.Tensor | None = None, stream=None) -
     return out
 
 
+def gdn_chunk_inverse(k: torch.Tensor, beta: torch.Tensor, g: torch.Tensor, out: torch.Tensor | None = None,
+                      stream=None) -> torch.Tensor:
+    """The chunk's A built from the gated-delta-rule inputs and inverted in one kernel
+    (qhtp_gdn_chunk_inverse; Stage A of gdn_chunk, scripts/gdn_ref_kernel.py:66-82): raw keys k bf16
+    [..., 256, 128], beta and per-token log gates g float32 [..., 256] -> T = (I - A)^-1 float32
+    [..., 256, 256]."""
+    if k.dtype != torch.bfloat16 or not k.is_cuda or not k.is_contiguous():
+        raise TypeError("k must be a contiguous CUDA bfloat16 tensor")
+    if k.dim() < 2 or k.shape[-2] != 256 or k.shape[-1] != 128:
+        raise ValueError("k must be [..., 256, 128]")
+    lead = k.shape[:-1]
+    for name, t in (("beta", beta), ("g", g)):
+        if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous() or t.shape != lead:
+            raise TypeError(f"{name} must be a contiguous CUDA float32 tensor of shape {tuple(lead)}")
+    n = k.numel() // (256 * 128)
+    shape = (*k.shape[:-2], 256, 256)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=k.device)
+    elif out.shape != shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("bad output tensor")
+    L.check("qhtp_gdn_chunk_inverse", L.lib.qhtp_gdn_chunk_inverse(
+        k.data_ptr(), beta.data_ptr(), g.data_ptr(), out.data_ptr(), n, 256, 128, _stream(stream)))
+    return out
+
+
 def gdn_solve_u16(A: torch.Tensor, *, zpA: int, sA: float, zpT: int, sT: float, out: torch.Tensor | None = None,
                   stream=None) -> torch.Tensor:
     """GdnSolve on u16 codes: value = (code - zp) * scale for A and T (gdn_solve_oc_check.py:28-29)."""

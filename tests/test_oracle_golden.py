@@ -6,6 +6,7 @@ reference's inputs bit for bit and that the exact requant model reproduces the r
 ``output_ref_q`` on every case of every promoted family.
 """
 import json
+from pathlib import Path
 from fractions import Fraction
 
 import numpy as np
@@ -193,3 +194,12 @@ def test_quantize_weight_fast_matches_loop(family):
     a, b = O.quantize_weight(fam, w), O.quantize_weight_fast(fam, w)
     for key in a:
         np.testing.assert_array_equal(a[key], b[key], err_msg=key)
+
+
+def test_gdn_A_from_kbg_matches_reference_chunk_kernel():
+    """chunk_A_from_kbg + inverse_fp64 reproduce the T the reference's own gdn_chunk forms
+    (scripts/gdn_ref_kernel.py, fp64; fixture by tests/golden/make_gdn_kbg_golden.py)."""
+    z = np.load(Path(__file__).parent / "golden" / "gdn_kbg_kat.npz")
+    A = G.chunk_A_from_kbg(z["k"], z["beta"], z["g_tok"])
+    T = G.inverse_fp64(A)
+    assert np.abs(T - z["T"]).max() < 1e-12
