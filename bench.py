@@ -41,10 +41,11 @@ L2_FLUSH_BYTES = 256 << 20
 # `ncu --set full` capture of this script's own workload (bench.py --steps 1 --warmup 3 ...); the
 # GDN figure is a 1024-chunk capture scaled by the chunk count to the 4096-chunk launch
 NCU_TRAFFIC_BYTES = {
-    ("qgemm", 4096, 4096, 14336): 155_152_640 + 101_383_680,          # full-size capture
+    ("qgemm", 4096, 4096, 14336): 152_121_856 + 98_887_424,           # full-size capture
     ("gdn", 4096): 4 * (100_822_016 + 208_797_696),                    # 1024-chunk capture x 4 chunks
-    ("qdecode", 16, 4096, 14336): 118_095_360 + 3_455_744,             # full-size capture
-    ("qdecode", 1, 4096, 4096): 33_754_112 + 0,                        # full-size capture
+    ("gdn_fused", 4096): 4 * (69_343_232 + 208_418_304),               # 1024-chunk capture x 4 chunks
+    ("qdecode", 16, 4096, 14336): 118_091_264 + 4_662_784,             # full-size capture
+    ("qdecode", 1, 4096, 4096): 33_753_344 + 0,                        # full-size capture
 }
 
 
@@ -467,6 +468,7 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
     bf = n_chunks * (C * 128 * 2 + C * 4 * 2 + C * C * 4)
     res["fused_A"] = {"metric": "gdn_chunk_inverse_chunks_per_s", "value": n_chunks * world / tf,
                       "ms_per_step": tf * 1e3, "hbm_gbs": bf / tf / 1e9, "hbm_frac": bf / tf / 1e9 / pk["hbm_gbs"],
+                      "traffic": NCU_TRAFFIC_BYTES.get(("gdn_fused", n_chunks)),
                       "kernel": "gdn256f_kernel (Gram MMAs + A epilogue + the C=256 inverse)",
                       "note": "k bf16 [C,128], beta and log gates f32 [C] -> T f32: algorithmic bytes 256C + 8C + 4C^2 "
                               "per chunk; A (bf16 [C,C]) never written or read"}
