@@ -410,8 +410,13 @@ def run_decode(args, world, rank, local, stream, shapes=None) -> list:
             t = max_over_ranks(statistics.mean(times), world)   # the event clock ticks in ~1 us steps
             alg = m * k * 2 + n * k // 2 + n * (k // blk) + n * 8 + m * n * 2
             read = int(op.plan.plane_bytes) + n * 32 + m * k * 2 + m * n * 2
+            # the library's dispatch: the channel-major decode kernel up to 64 rows, and up to 128 rows
+            # when the channel tiles leave room for a K split; else the row-tiled GEMM
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            row_tiled = m > 64 and 2 * ((n + 127) // 128) > sms
             rows.append({"m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
-                         "kernel": "split_u16_planes + qdecode_kernel (channel-major, cluster split-K)",
+                         "kernel": "split_u16_planes + " + ("qgemm_kernel (row tiles)" if row_tiled else
+                                                            "qdecode_kernel (channel-major, cluster split-K)"),
                          "alg_bytes": alg, "alg_gbs": round(alg / t / 1e9, 1),
                          "alg_frac": round(alg / t / 1e9 / pk["hbm_gbs"], 3),
                          "read_bytes": read, "read_gbs": round(read / t / 1e9, 1),
