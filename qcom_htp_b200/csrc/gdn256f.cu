@@ -92,6 +92,34 @@ __device__ __forceinline__ void build_a32(uint32_t taddr, int i, int j0, uint8_t
   put_row_bf16(img, r, c0 >> 3, v);
 }
 
+// The k images hold the key rows in 32-row blocks ordered 0, 1, 2, 3, 7, 6, 5, 4: the Gram rows of
+// TMEM lane quadrant q are then key blocks q (top half) and 7 - q (bottom half), whose
+// below-diagonal work (q + 1 and 8 - q blocks of 32 columns) adds up to 9 blocks in every quadrant.
+__host__ __device__ __forceinline__ int kb_of_image(int p) { return p < 4 ? p : 11 - p; }
+
+// Where A's 32 x 32 block (key row block rb, key column block cb <= rb) goes: the image the inverse
+// reads it from, the image row of its first row, and the image column of its first column.
+//   rb, cb in the same 64-block q:   AU[q] (rb even) / AL[q] (rb odd), columns 32 * (cb - 2q)
+//   rb, cb in the same 128-block h:  A2[h], rows 32 * (rb - 4h - 2), columns 32 * (cb - 4h)
+//   otherwise (rb >= 4, cb <= 3):    A3 K-region cb / 2, rows 32 * (rb - 4), columns 32 * (cb % 2)
+__device__ __forceinline__ uint32_t a_block_image(int rb, int cb, int& r0, int& c0) {
+  if ((rb >> 1) == (cb >> 1)) {
+    const int q = rb >> 1;
+    r0 = 0;
+    c0 = 32 * (cb - 2 * q);
+    return kAUL + ((rb & 1) ? kAL : kAU) + q * kTile;
+  }
+  if ((rb >> 2) == (cb >> 2)) {
+    const int h = rb >> 2;
+    r0 = 32 * (rb - 4 * h - 2);
+    c0 = 32 * (cb - 4 * h);
+    return kA2 + h * 8 * KB;
+  }
+  r0 = 32 * (rb - 4);
+  c0 = 32 * (cb & 1);
+  return kA3 + (cb >> 1) * 16 * KB;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gdn256f_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmT,
                    const GdnKbgArgs args) {
@@ -139,8 +167,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto issue_kbg = [&](int64_t ch, uint32_t parity) {
     mbar_arrive_expect_tx(k_bar, kKBytes);
     const int y0 = static_cast<int>(ch * kC);
-    tma_load_2d(sm + kK, &tmK, k_bar, 0, y0);
-    tma_load_2d(sm + kK + 32 * KB, &tmK, k_bar, 64, y0);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int p = 0; p < 8; ++p)  // image block p holds key rows 32 * kb_of_image(p) ..
+        tma_load_2d(sm + kK + h * 32 * KB + p * kTile, &tmK, k_bar, 64 * h, y0 + 32 * kb_of_image(p));
     bulk_load(sm + kBGL, args.beta + ch * kC, kC * 4, k_bar);
     bulk_load(sm + kBGL + KB, args.g + ch * kC, kC * 4, k_bar);
     pend = true;
@@ -198,7 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ss = fmaf(hi, hi, ss);
           }
         }
-      rn[tid] = rsqrtf(ss + 1e-6f);  // the reference's l2norm: x / sqrt(sum x^2 + 1e-6)
+      // the reference's l2norm: x / sqrt(sum x^2 + 1e-6); image row tid holds key row
+      // 32 * kb_of_image(tid / 32) + tid % 32
+      rn[32 * kb_of_image(tid >> 5) + (tid & 31)] = rsqrtf(ss + 1e-6f);
       be[tid] = reinterpret_cast<const float*>(sm + kBGL)[tid];
       if (warp == 0) {
         const float* gl = reinterpret_cast<const float*>(sm + kBGL + KB);
@@ -233,42 +266,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- B1: Gram rows -> the A images (AU / AL: the diagonal 64x64 blocks, A2: the level-2 blocks,
     // A3: rows 128..255 x columns 0..127).  Warp (qd, half) owns Gram rows 32qd + lane of each half.
     if (ok) {
+      // Quadrant qd's 9 blocks of 32 Gram columns, alternately to its two warps: key row block qd
+      // (TMEM columns = key columns 32 cb, cb = 0..qd), then key row block 7 - qd (TMEM column 128 +
+      // image column of key block cb, cb = 0..7-qd).  Blocks wholly above the diagonal never occur.
       const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
-      {  // rows 0..127 (Gram columns 0..127)
-        const int i = 32 * qd + lane;
-        const float bi = be[i] * rn[i], gi = gc[i];
-        if (qd < 2) {  // block 0: AU[0] (rows 0..31) / AL[0] (rows 32..63), columns 0..63
-          build_a32(tl + 32 * half, i, 32 * half, aul + (qd ? kAL : kAU), lane, 32 * half, bi, gi, rn, gc);
-        } else if (half == 0) {  // A2[0]: rows 64..127, columns 0..63
-#pragma unroll
-          for (int j = 0; j < 2; ++j) build_a32(tl + 32 * j, i, 32 * j, sm + kA2, i - 64, 32 * j, bi, gi, rn, gc);
-        } else {  // block 1: AU[1] (rows 64..95) / AL[1] (rows 96..127), columns 64..127
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            build_a32(tl + 64 + 32 * j, i, 64 + 32 * j, aul + (qd == 2 ? kAU : kAL) + kTile, lane, 32 * j, bi, gi, rn, gc);
-        }
-      }
-      {  // rows 128..255 (Gram column j at TMEM column 128 + j)
-        const int i = 128 + 32 * qd + lane;
-        const float bi = be[i] * rn[i], gi = gc[i];
-        const uint32_t t2 = tl + 128;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)  // A3 K-region `half`: columns 64*half..64*half+63
-          build_a32(t2 + 64 * half + 32 * j, i, 64 * half + 32 * j, sm + kA3 + half * 16 * KB, i - 128, 32 * j, bi, gi,
-                    rn, gc);
-        if (qd < 2) {  // block 2: AU[2] (rows 128..159) / AL[2] (rows 160..191), columns 128..191
-          build_a32(t2 + 128 + 32 * half, i, 128 + 32 * half, aul + (qd ? kAL : kAU) + 2 * kTile, lane, 32 * half, bi,
-                    gi, rn, gc);
-        } else if (half == 0) {  // A2[1]: rows 192..255, columns 128..191
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            build_a32(t2 + 128 + 32 * j, i, 128 + 32 * j, sm + kA2 + 8 * KB, i - 192, 32 * j, bi, gi, rn, gc);
-        } else {  // block 3: AU[3] (rows 192..223) / AL[3] (rows 224..255), columns 192..255
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            build_a32(t2 + 192 + 32 * j, i, 192 + 32 * j, aul + (qd == 2 ? kAU : kAL) + 3 * kTile, lane, 32 * j, bi, gi,
-                      rn, gc);
-        }
+#pragma unroll 1
+      for (int idx = half; idx < 9; idx += 2) {
+        const bool top = idx <= qd;
+        const int rb = top ? qd : 7 - qd;
+        const int cb = top ? idx : idx - qd - 1;
+        const int icol = 32 * (cb < 4 ? cb : 11 - cb);  // image column of key block cb
+        const int i = 32 * rb + lane;
+        int r0, c0;
+        const uint32_t img = a_block_image(rb, cb, r0, c0);
+        build_a32(tl + (top ? 0u : 128u) + static_cast<uint32_t>(icol), i, 32 * cb, sm + img, r0 + lane, c0,
+                  be[i] * rn[i], gc[i], rn, gc);
       }
     }
     fence_proxy_async_smem();
@@ -560,8 +572,8 @@ cudaError_t launch_gdn256_fused(const void* k, const float* beta, const float* g
   }
   CUtensorMap tk, tt;
   const uint64_t rows = static_cast<uint64_t>(n_chunks) * kC;
-  // k [n_chunks * 256, 128] bf16: boxes of 64 Dk columns (128 bytes, the swizzle span) x 256 rows
-  if (!make_tmap_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 128, rows, 128 * 2, 64, 256)) return cudaErrorInvalidValue;
+  // k [n_chunks * 256, 128] bf16: boxes of 64 Dk columns (128 bytes, the swizzle span) x 32 rows
+  if (!make_tmap_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 128, rows, 128 * 2, 64, 32)) return cudaErrorInvalidValue;
   if (!make_tmap_2d(&tt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, T, kC, rows, kC * 4, 32, 32)) return cudaErrorInvalidValue;
   const int64_t grid = n_chunks < sms[dev] ? n_chunks : sms[dev];
   GdnKbgArgs args{T, beta, g, n_chunks, err_ptr[dev]};
