@@ -63,3 +63,11 @@ def test_decode_repeat_and_twin_calls_identical():
     a = run_case(c, op=op)
     b = run_case(c, op=op)
     np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("m", [64, 65, 128])
+def test_dispatch_boundary_wide_n(m):
+    """At N = 14336 (112 channel tiles) rows 65..128 go to the row-tiled kernel and up to 64 to the
+    channel-major one; both sides of the boundary must give the oracle's bytes."""
+    c = O.make_baseline_case("w4a16_lpbq", m, 512, 14336, seed=0xD15 + m)
+    np.testing.assert_array_equal(run_case(c), O.exact_output(c))
