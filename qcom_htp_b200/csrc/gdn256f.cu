@@ -195,13 +195,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
 
-    // ---- B0: this chunk's k, beta and log gates have landed.  Thread 0 issues the Gram MMAs
-    // (both operands the K-major images of k); meanwhile every thread forms 1/|k_i| of row i = tid,
-    // copies beta_i out of the load area, and warp 0 forms g = cumsum of the log gates.
+    // ---- B0: this chunk's k, beta and log gates have landed.  Warp 1 lane 0 issues the Gram MMAs
+    // (both operands the K-major images of k); meanwhile every thread forms 1/|k| of its image row,
+    // copies beta_i out of the load area, and warp 2 forms g = cumsum of the log gates (the MMAs are
+    // issued from warp 1, so no warp carries more than one of these jobs besides its norms).
     bool ok = mbar_wait(k_bar, it & 1, err, kErrTimeoutFull);
     if (ok) {
-      if (tid == 0) {
-        pend = false;
+      if (tid == 0) pend = false;
+      if (tid == 32) {
         tc_fence_after();
 #pragma unroll
         for (int h = 0; h < 2; ++h)
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 32 * kb_of_image(tid / 32) + tid % 32
       rn[32 * kb_of_image(tid >> 5) + (tid & 31)] = rsqrtf(ss + 1e-6f);
       be[tid] = reinterpret_cast<const float*>(sm + kBGL)[tid];
-      if (warp == 0) {
+      if (warp == 2) {
         const float* gl = reinterpret_cast<const float*>(sm + kBGL + KB);
         float x[8], run = 0.0f;
 #pragma unroll
