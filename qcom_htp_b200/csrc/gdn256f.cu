@@ -82,12 +82,20 @@ __device__ __forceinline__ void build_a32(uint32_t taddr, int i, int j0, uint8_t
                                           float gi, const float* rn, const float* gc) {
   uint32_t v[32];
   tmem_ld32(taddr, v);
+  // the group's column constants: j0 is a multiple of 32, so 16-byte broadcast loads
+  const float4* rn4 = reinterpret_cast<const float4*>(rn + j0);
+  const float4* gc4 = reinterpret_cast<const float4*>(gc + j0);
   tmem_ld_wait();
 #pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const int j = j0 + e;
-    const float a = i > j ? -(bi_rn * rn[j]) * __uint_as_float(v[e]) * exp2_ftz(gi - gc[j]) : 0.0f;
-    v[e] = __float_as_uint(a);
+  for (int e4 = 0; e4 < 8; ++e4) {
+    const float4 rj = rn4[e4], gj = gc4[e4];
+    const float rr[4] = {rj.x, rj.y, rj.z, rj.w}, gg[4] = {gj.x, gj.y, gj.z, gj.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = 4 * e4 + u;
+      const float a = i > j0 + e ? -(bi_rn * rr[u]) * __uint_as_float(v[e]) * exp2_ftz(gi - gg[u]) : 0.0f;
+      v[e] = __float_as_uint(a);
+    }
   }
   put_row_bf16(img, r, c0 >> 3, v);
 }
