@@ -78,6 +78,7 @@ __device__ __forceinline__ float exp2_ftz(float x) {
 // columns c0..c0+31 of a swizzled image:  A = -beta_i / |k_i| * (k_i . k_j) / |k_j| * exp(g_i - g_j)
 // below the diagonal, 0 on and above it; the decay is 2^(g2_i - g2_j) with g2 = g * log2(e), one SFU
 // instruction per entry.  All lanes read the same column constants (broadcast).
+template <bool DIAG>
 __device__ __forceinline__ void build_a32(uint32_t taddr, int i, int j0, uint8_t* img, int r, int c0, float bi_rn,
                                           float gi, const float* rn, const float* gc) {
   uint32_t v[32];
@@ -93,7 +94,8 @@ __device__ __forceinline__ void build_a32(uint32_t taddr, int i, int j0, uint8_t
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int e = 4 * e4 + u;
-      const float a = i > j0 + e ? -(bi_rn * rr[u]) * __uint_as_float(v[e]) * exp2_ftz(gi - gg[u]) : 0.0f;
+      float a = -(bi_rn * rr[u]) * __uint_as_float(v[e]) * exp2_ftz(gi - gg[u]);
+      if constexpr (DIAG) a = i > j0 + e ? a : 0.0f;  // the diagonal block: strictly lower part only
       v[e] = __float_as_uint(a);
     }
   }
@@ -288,8 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = 32 * rb + lane;
         int r0, c0;
         const uint32_t img = a_block_image(rb, cb, r0, c0);
-        build_a32(tl + (top ? 0u : 128u) + static_cast<uint32_t>(icol), i, 32 * cb, sm + img, r0 + lane, c0,
-                  be[i] * rn[i], gc[i], rn, gc);
+        const uint32_t ta = tl + (top ? 0u : 128u) + static_cast<uint32_t>(icol);
+        if (cb == rb)  // warp-uniform
+          build_a32<true>(ta, i, 32 * cb, sm + img, r0 + lane, c0, be[i] * rn[i], gc[i], rn, gc);
+        else
+          build_a32<false>(ta, i, 32 * cb, sm + img, r0 + lane, c0, be[i] * rn[i], gc[i], rn, gc);
       }
     }
     fence_proxy_async_smem();
