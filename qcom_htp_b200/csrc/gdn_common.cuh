@@ -102,14 +102,14 @@ __device__ __forceinline__ void codes_to_bf16(uint8_t* p, const InCodes& ic) {
 // Level 0: forward substitution on one 32x32 diagonal block held in a swizzled bf16 tile (rows 0..31,
 // columns chunk_off*8 .. chunk_off*8+31).  Lane j computes column j:
 //     t[i] = delta(i, j) + sum_{k<i} A[i][k] * t[k]
-// with two partial sums (even / odd k) to halve the dependency chain.  Entries with k >= i are
+// with four partial sums (k mod 4) to shorten the dependency chain.  Entries with k >= i are
 // never read.  t[i] is exactly 0 for i < j and exactly 1 for i == j.
 template <bool U16>
 __device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off, int lane, float (&t)[32],
                                              const InCodes& ic) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    float s0 = (i == lane) ? 1.0f : 0.0f, s1 = 0.0f;
+    float s[4] = {(i == lane) ? 1.0f : 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       if (8 * c < i) {
@@ -120,15 +120,12 @@ __device__ __forceinline__ void solve_diag32(const uint8_t* tile, int chunk_off,
           const int k = 8 * c + e;
           if (k < i) {
             const float a = (e & 1) ? in_hi<U16>(w[e >> 1], ic) : in_lo<U16>(w[e >> 1], ic);
-            if (e & 1)
-              s1 = fmaf(a, t[k], s1);
-            else
-              s0 = fmaf(a, t[k], s0);
+            s[k & 3] = fmaf(a, t[k], s[k & 3]);
           }
         }
       }
     }
-    t[i] = s0 + s1;
+    t[i] = (s[0] + s[1]) + (s[2] + s[3]);
   }
 }
 
