@@ -43,7 +43,7 @@ L2_FLUSH_BYTES = 256 << 20
 NCU_TRAFFIC_BYTES = {
     ("qgemm", 4096, 4096, 14336): 152_121_856 + 98_887_424,           # full-size capture
     ("gdn", 4096): 4 * (100_822_016 + 208_797_696),                    # 1024-chunk capture x 4 chunks
-    ("gdn_fused", 4096): 4 * (69_306_112 + 207_934_208),               # 1024-chunk capture x 4 chunks
+    ("gdn_fused", 4096): 4 * (69_339_904 + 208_701_952),               # 1024-chunk capture x 4 chunks
     ("qdecode", 16, 4096, 14336): 118_091_264 + 4_662_784,             # full-size capture
     ("qdecode", 1, 4096, 4096): 33_753_344 + 0,                        # full-size capture
 }
