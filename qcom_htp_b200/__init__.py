@@ -7,6 +7,7 @@ that library is missing -- there is no CPU fallback.
 """
 from . import _lib  # noqa: F401  (loads libqhtp.so or raises)
 from ._lib import QhtpError
+from . import ops  # noqa: F401  (registers torch.ops.qhtp.*)
 from .gdn import gdn_chunk_inverse, gdn_inverse, gdn_solve_u16, gdnbm_solve
 from .matmul import (QuantMatMul, hmx_u8i4_to_u8_matmul, hmx_u8i8_to_u8_matmul, hmx_u16i4_to_u16_matmul,
                      hmx_u16i8_to_u16_matmul, hmx_u16i16_to_u16_matmul, lpbq_expand_i8, weights_from_wire)
