@@ -130,3 +130,21 @@ def test_exact_tie_half_even(L):
     assert requant_code_host(10 ** 6, *c, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == 255
     assert requant_code_host(-7, *c, 1, -53, 1 << 52, 1 << 52, -52, 128, 255) == 124   # 128 - 3.5 -> 124
     assert requant_code_host(5, 1 << 52, 33, 1, -53, 1 << 52, 1 << 52, -52, 0, 255) == -1   # bad shift
+
+
+def test_host_run_rejects_small_workspace_before_any_device_work(L):
+    """qhtp_matmul_run_host validates sizes on the host: a workspace below
+    qhtp_matmul_workspace_bytes(plan, chunk rows) is INVALID_ARGUMENT with a message, before any
+    device pointer is touched (the pointers below are never dereferenced)."""
+    p = L.QhtpMatmulPlan()
+    assert L.lib.qhtp_matmul_plan(C.byref(_weights(L)), C.byref(p)) == L.OK
+    p.prepared = 4096                                  # stands in for a prepared buffer
+    fake = C.c_void_p(1 << 20)                         # 256-byte aligned, never dereferenced
+    used = C.c_uint32(0)
+    need = L.lib.qhtp_matmul_workspace_bytes(C.byref(p), 512)
+    st = L.lib.qhtp_matmul_run_host(C.byref(p), fake, 4096, fake, fake, fake, fake, need - 1, 512, C.byref(used),
+                                    None)
+    assert st == L.INVALID_ARGUMENT
+    assert b"workspace" in L.lib.qhtp_last_error_string()
+    assert L.lib.qhtp_matmul_run_host(C.byref(p), None, 4096, fake, fake, fake, fake, need, 512, None,
+                                      None) == L.INVALID_ARGUMENT
