@@ -61,8 +61,11 @@ typedef enum QhtpFamily {
 
 typedef enum QhtpWeightSchema {
   QHTP_SCHEMA_PER_CHANNEL = 0, /* symmetric per-output-channel scale                         */
-  QHTP_SCHEMA_LPBQ = 1         /* int4 x per-block uint8 factor (1..16) x per-channel scale;  */
+  QHTP_SCHEMA_LPBQ = 1,        /* int4 x per-block uint8 factor (1..16) x per-channel scale;  */
                                /* expanded exactly like HmxW4LpbqExpandToI8Op.cpp:94-97        */
+  QHTP_SCHEMA_PER_GROUP = 2    /* W4 families only: float32 scale per (channel, 64 weights of  */
+                               /* K), float32 bias; scripts/generate_qnn_matmul_python_cases.py */
+                               /* :392-423 (weights) and :460-470 (bias kept float)             */
 } QhtpWeightSchema;
 
 typedef enum QhtpDequant {
@@ -76,7 +79,10 @@ typedef enum QhtpDequant {
  *   W4A8, W4A16 : int4 K-pair bytes [K/2, N]: byte (k>>1)*N + n, even k in the low nibble,
  *                 two's-complement nibbles (HmxW4LpbqExpandToI8Op.cpp:5,32-40)
  *   W16A16      : int16 [N, K] row-major
- * lpbq_block_scale: uint8 [N, K/lpbq_block] (n*(K/lpbq_block) + kb), LPBQ only, else NULL. */
+ * lpbq_block_scale: uint8 [N, K/lpbq_block] (n*(K/lpbq_block) + kb), LPBQ only, else NULL.
+ * QHTP_SCHEMA_PER_GROUP: weight_scale is float32 [N, K/64] (n*(K/64) + g), K a multiple of 64 and
+ * above 64, dequant QHTP_DEQUANT_F32_WEIGHT; bias_q is unused and bias_float (float32 [N]) is the
+ * bias, added in float64 like the reference (y = x_deq @ w_deq.T + bias). */
 typedef struct QhtpMatmulWeights {
   uint32_t family;      /* QhtpFamily       */
   uint32_t schema;      /* QhtpWeightSchema */
@@ -92,6 +98,7 @@ typedef struct QhtpMatmulWeights {
   int32_t act_offset;                /* QNN offset = -zero_point (-128 for u8, -32768 for u16) */
   double out_scale;
   int32_t out_offset;                /* 0 for u8 outputs, -32768 for u16 outputs */
+  const float *bias_float;           /* [N] float32, QHTP_SCHEMA_PER_GROUP only, else NULL */
 } QhtpMatmulWeights;
 
 /* Host-side plan: filled by qhtp_matmul_plan (host only) and bound to a prepared device buffer by

@@ -543,6 +543,43 @@ def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
     return out
 
 
+def per_group_output(case: QuantCase) -> np.ndarray:
+    """Output codes of the per-group W4 schema (generate_qnn_matmul_python_cases.py:392-423 weights,
+    :460-470 float bias, :472-481 output), in the operation order the GPU uses.
+
+    The reference computes y = x_deq @ w_deq.T + bias in float64 with w_deq = float32(q*s[n,g]).
+    Each group scale is s = m*2**e, so float32(q*s) = (q*m + e')*2**e exactly (e' = residual_plane
+    per group), and a group's contribution to a row is the exact integer
+
+        Z[g] = m*sum_g((x-zp)*q) + sum_g((x-zp)*e')          times 2**e[n,g].
+
+    Here acc = sum over g in K order of Z[g]*2**e (each term exact, one float64 rounding per
+    addition), y = act_scale*acc + float64(bias), out = clip(rint(y/out_scale + zp_O)).  This
+    sequence reproduces the reference's output_ref_q on its per-group golden cases (the reference
+    sums inexact float64 products in BLAS order; the two agree except within float64 rounding of a
+    tie)."""
+    fam = case.family
+    if fam.schema != "per_group":
+        raise ValueError("per_group_output: per-group families only")
+    q = case.weight_q.astype(np.int64)
+    n, k = q.shape
+    g_count = k // 64
+    m_s, e_s = split_f32(case.weight_scale)                   # [N, G]
+    p = (q.reshape(n, g_count, 64) * m_s[:, :, None]).reshape(n, k)
+    ep = round_to_24_bits(p) - p                              # e' per group, |e'| <= 8
+    xz = (case.act_q.astype(np.int64) - fam.act_zp).astype(np.float64)
+    acc = np.zeros((case.act_q.shape[0], n))
+    for g in range(g_count):
+        sl = slice(64 * g, 64 * (g + 1))
+        sq = (xz[:, sl] @ q[:, sl].astype(np.float64).T).astype(np.int64)   # exact: |.| < 2**53
+        se = (xz[:, sl] @ ep[:, sl].astype(np.float64).T).astype(np.int64)
+        z = m_s[None, :, g] * sq + se
+        acc = acc + np.ldexp(z.astype(np.float64), e_s[None, :, g])
+    y = case.act_scale * acc + case.bias_float.astype(np.float64)[None, :]
+    r = np.rint(y / case.out_scale + fam.out_zp)
+    return np.clip(r, 0, fam.out_qmax).astype(fam.out_dtype)
+
+
 def integer_accumulator(case: QuantCase) -> np.ndarray:
     """sum_k (x_q - zp) * q as int64 -- the W16A16 identity target."""
     xc = case.act_q.astype(np.int64) - case.family.act_zp

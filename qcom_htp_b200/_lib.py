@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libqhtp.so"
 OK, INVALID_ARGUMENT, UNSUPPORTED, RUNTIME_ERROR = 0, 1, 2, 3
 
 FAMILY = {"u8i8": 0, "w4a8": 1, "w8a16": 2, "w4a16": 3, "w16a16": 4}
-SCHEMA = {"per_channel": 0, "lpbq": 1}
+SCHEMA = {"per_channel": 0, "lpbq": 1, "per_group": 2}
 DEQUANT = {"f32": 0, "exact": 1}
 
 
@@ -25,6 +25,7 @@ class QhtpMatmulWeights(C.Structure):
         ("lpbq_block_scale", C.c_void_p),
         ("act_scale", C.c_double), ("act_offset", C.c_int32),
         ("out_scale", C.c_double), ("out_offset", C.c_int32),
+        ("bias_float", C.c_void_p),
     ]
 
 

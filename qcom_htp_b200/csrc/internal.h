@@ -15,6 +15,8 @@ enum GemmMode : uint32_t {
   kModeF32 = 0,    // f32 weight dequant: B tile = [q (128 ch) | e' (128 ch)], s8
   kModeExact = 1,  // exact dequant, 8-bit weights: B tile = q (128 ch), s8
   kModeW16 = 2,    // exact dequant, int16 weights: B tile = [hi s8 (128 ch) | lo u8 (128 ch)]
+  kModeGroup = 3,  // per-group W4 (float32 scale per 64 weights of K): tiles of 64 channels,
+                   // B tile = [q (64 ch) | e' (64 ch)], s8; qgroup.cu
 };
 
 constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
@@ -22,7 +24,18 @@ constexpr int kTileN = 128;      // output channels per tile
 constexpr int kTileK = 128;      // bytes of K per pipeline stage (one 128-byte swizzle row)
 
 // weight-plane rows per tile in the prepared layout
-inline constexpr uint32_t b_rows_for_mode(uint32_t mode) { return mode == kModeExact ? 128u : 256u; }
+inline constexpr uint32_t b_rows_for_mode(uint32_t mode) {
+  return mode == kModeExact || mode == kModeGroup ? 128u : 256u;
+}
+
+// Per-group schema: channels per tile, and the constants of one (tile, group) in the prepared
+// buffer: czp int64[64] = zp*(m*sum q + sum e') | 2^e float64[64] | m int32[64]
+constexpr int kGroupTileN = 64;
+constexpr int kGroupRecBytes = kGroupTileN * (8 + 8 + 4);
+inline size_t group_rec_bytes(const QhtpMatmulPlan* p) {
+  const size_t b = static_cast<size_t>(p->n_tiles) * (p->k_pad / kTileK) * 2 * kGroupRecBytes;
+  return (b + 255) / 256 * 256;
+}
 
 struct ChannelRecord {  // 32 bytes, one per output channel (padded to the tile)
   int64_t beff;         // effective bias, in accumulator units
@@ -58,6 +71,10 @@ bool decode_supported(const QhtpMatmulPlan* plan, uint32_t m);
 cudaError_t launch_decode(const GemmLaunch& g, const uint8_t* a_base);
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
                            int* bad_scale, cudaStream_t stream);
+// qgroup.cu: the per-group W4 schema (prepare, and the GEMM on the u8 activation or byte planes)
+cudaError_t launch_prepare_group(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
+                                 int* bad_scale, cudaStream_t stream, int sms);
+cudaError_t launch_gemm_group(const GemmLaunch& g, const uint8_t* a_base, uint64_t a_rows, int sms);
 cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k, uint32_t n, uint32_t block,
                                int8_t* out, cudaStream_t stream);
 

@@ -571,6 +571,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
     a_base = static_cast<const uint8_t*>(g.act);
     a_rows = g.m;
   }
+  if (pl->mode == kModeGroup) return launch_gemm_group(g, a_base, a_rows, sm_count());
   if (decode_supported(pl, g.m)) return launch_decode(g, a_base);
   if (!make_tmap_2d_u8(&ta, a_base, K, a_rows, K, kTileK, kTileM)) return cudaErrorInvalidValue;
   const uint32_t brows = b_rows_for_mode(pl->mode);
@@ -732,6 +733,7 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
 
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared, int* bad_scale,
                            cudaStream_t stream) {
+  if (plan->mode == kModeGroup) return launch_prepare_group(plan, w, prepared, bad_scale, stream, sm_count());
   uint8_t* base = static_cast<uint8_t*>(prepared);
   long long* sums = reinterpret_cast<long long*>(base + plan->plane_bytes + plan->record_bytes);
   cudaError_t e = cudaMemsetAsync(base, 0, plan->prepared_bytes, stream);

@@ -155,7 +155,8 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   QhtpMatmulPlan p;
   std::memset(&p, 0, sizeof(p));
   if (!family_bits(w->family, &p.act_bits, &p.weight_bits, &p.out_bits)) return QHTP_STATUS_INVALID_ARGUMENT;
-  if (w->schema != QHTP_SCHEMA_PER_CHANNEL && w->schema != QHTP_SCHEMA_LPBQ) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (w->schema != QHTP_SCHEMA_PER_CHANNEL && w->schema != QHTP_SCHEMA_LPBQ && w->schema != QHTP_SCHEMA_PER_GROUP)
+    return QHTP_STATUS_INVALID_ARGUMENT;
   if (w->dequant != QHTP_DEQUANT_F32_WEIGHT && w->dequant != QHTP_DEQUANT_EXACT) return QHTP_STATUS_INVALID_ARGUMENT;
   if (w->k == 0 || w->n == 0) return QHTP_STATUS_INVALID_ARGUMENT;
   if (w->k % 32 || w->n % 32) return QHTP_STATUS_UNSUPPORTED;     // reference: M/K/N multiples of 32
@@ -164,6 +165,10 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
     if (p.weight_bits != 4) return QHTP_STATUS_UNSUPPORTED;
     if (w->lpbq_block == 0 || w->lpbq_block % 32 || w->k % w->lpbq_block || w->k <= w->lpbq_block)
       return QHTP_STATUS_UNSUPPORTED;
+  }
+  if (w->schema == QHTP_SCHEMA_PER_GROUP) {  // generate_qnn_matmul_python_cases.py:392-396
+    if (p.weight_bits != 4 || w->dequant != QHTP_DEQUANT_F32_WEIGHT) return QHTP_STATUS_UNSUPPORTED;
+    if (w->k % 64 || w->k <= 64) return QHTP_STATUS_UNSUPPORTED;
   }
   if (p.weight_bits == 16 && w->dequant != QHTP_DEQUANT_EXACT) return QHTP_STATUS_UNSUPPORTED;
   if (!(w->act_scale > 0.0) || !std::isfinite(w->act_scale) || !(w->out_scale > 0.0) ||
@@ -182,7 +187,10 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   p.n = w->n;
   p.lpbq_block = w->schema == QHTP_SCHEMA_LPBQ ? w->lpbq_block : 0;
   p.a_planes = p.act_bits == 16 ? 2 : 1;
-  if (p.weight_bits == 16) {
+  if (w->schema == QHTP_SCHEMA_PER_GROUP) {
+    p.mode = kModeGroup;
+    p.ch_per_tile = kGroupTileN;
+  } else if (p.weight_bits == 16) {
     p.mode = kModeW16;
     p.ch_per_tile = 128;
   } else if (w->dequant == QHTP_DEQUANT_F32_WEIGHT) {
@@ -200,7 +208,9 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   split_f64(w->out_scale, &p.out_mant, &p.out_exp2);
   p.plane_bytes = align_up(static_cast<size_t>(p.n_tiles) * b_rows_for_mode(p.mode) * p.k_pad, 256);
   const size_t npad = static_cast<size_t>(p.n_tiles) * p.ch_per_tile;
-  p.record_bytes = align_up(npad * sizeof(ChannelRecord), 256);
+  // per-group: the (tile, group) constant blocks, then the float64 bias per channel
+  p.record_bytes = p.mode == kModeGroup ? group_rec_bytes(&p) + align_up(npad * sizeof(double), 256)
+                                        : align_up(npad * sizeof(ChannelRecord), 256);
   // planes | records | per-channel sums (prepare scratch) | 256-byte status word area
   p.prepared_bytes = p.plane_bytes + p.record_bytes + align_up(npad * 16, 256) + 256;
   p.prepared = nullptr;
@@ -216,7 +226,9 @@ QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan* plan, const QhtpMatmulWeights* w,
   if (bytes < plan->prepared_bytes || !aligned(prepared, 256)) return QHTP_STATUS_INVALID_ARGUMENT;
   if (w->family != plan->family || w->k != plan->k || w->n != plan->n || w->schema != plan->schema)
     return QHTP_STATUS_INVALID_ARGUMENT;
-  if (w->weight == nullptr || w->weight_scale == nullptr || w->bias_q == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (w->weight == nullptr || w->weight_scale == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (plan->schema == QHTP_SCHEMA_PER_GROUP ? w->bias_float == nullptr : w->bias_q == nullptr)
+    return QHTP_STATUS_INVALID_ARGUMENT;
   if (plan->schema == QHTP_SCHEMA_LPBQ && w->lpbq_block_scale == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
   cudaStream_t s = as_stream(stream);
   // status word: last 256-byte area of the prepared buffer (zeroed by the prepare memset)
@@ -329,6 +341,7 @@ QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan* plan, void* workspace, uint32
 
 QhtpStatus qhtp_matmul_read_records(const QhtpMatmulPlan* plan, void* host_dst, size_t bytes, void* stream) {
   if (!plan_ok(plan) || plan->prepared == nullptr || host_dst == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
+  if (plan->mode == kModeGroup) return QHTP_STATUS_UNSUPPORTED;  // per-(channel, group) constants, no record
   const size_t need = static_cast<size_t>(plan->n_tiles) * plan->ch_per_tile * sizeof(ChannelRecord);
   if (bytes < need) return QHTP_STATUS_INVALID_ARGUMENT;
   cudaStream_t s = as_stream(stream);

@@ -50,19 +50,23 @@ class QuantMatMul:
     ----------
     family        "u8i8" | "w4a8" | "w8a16" | "w4a16" | "w16a16"
     weight        int8 [N,K] (8-bit), uint8 K-pair [K/2,N] (int4), int16 [N,K] (W16A16)
-    weight_scale  float32 [N] per-output-channel scale (LPBQ: the per-channel base scale)
-    bias_q        int32 [N], quantized at act_scale * weight_scale
+    weight_scale  float32 [N] per-output-channel scale (LPBQ: the per-channel base scale;
+                  per_group: float32 [N, K/64], one scale per 64 weights along K)
+    bias_q        int32 [N], quantized at act_scale * weight_scale (None for per_group)
+    bias_float    float32 [N], per_group only: the float bias the reference keeps unquantized
+                  (generate_qnn_matmul_python_cases.py:460-470)
     act_scale/out_scale, act_offset/out_offset  QNN affine parameters (offset = -zero_point);
                   offsets default to the family's fixed zero points (A8: 128, A16/out16: 32768, out8: 0)
-    schema        "per_channel" | "lpbq"; LPBQ needs lpbq_block_scale uint8 [N, K/lpbq_block]
+    schema        "per_channel" | "lpbq" | "per_group"; LPBQ needs lpbq_block_scale uint8 [N, K/lpbq_block];
+                  per_group (W4 families) needs K a multiple of 64 above 64
     dequant       "f32" (float32 weight dequant, the reference oracle's rule; default for 4/8-bit)
                   or "exact" (w*s exactly; the only mode for W16A16)
     """
 
-    def __init__(self, family: str, weight: torch.Tensor, weight_scale: torch.Tensor, bias_q: torch.Tensor, *,
-                 act_scale: float, out_scale: float, act_offset: int | None = None, out_offset: int | None = None,
+    def __init__(self, family: str, weight: torch.Tensor, weight_scale: torch.Tensor, bias_q: torch.Tensor | None,
+                 *, act_scale: float, out_scale: float, act_offset: int | None = None, out_offset: int | None = None,
                  schema: str = "per_channel", lpbq_block_scale: torch.Tensor | None = None, lpbq_block: int = 0,
-                 dequant: str | None = None, stream=None):
+                 dequant: str | None = None, bias_float: torch.Tensor | None = None, stream=None):
         if family not in FAMILY_BITS:
             raise ValueError(f"unknown family {family!r}")
         a_bits, w_bits, o_bits = FAMILY_BITS[family]
@@ -83,13 +87,20 @@ class QuantMatMul:
             want = torch.int16 if w_bits == 16 else torch.int8
         if weight.dtype != want:
             raise TypeError(f"{family}: weight must be {want}, got {weight.dtype}")
-        for name, t in (("weight", weight), ("weight_scale", weight_scale), ("bias_q", bias_q)):
+        if schema not in L.SCHEMA:
+            raise ValueError(f"unknown schema {schema!r}")
+        per_group = schema == "per_group"
+        bias_t = bias_float if per_group else bias_q
+        if bias_t is None:
+            raise ValueError("per_group needs bias_float" if per_group else "bias_q is required")
+        for name, t in (("weight", weight), ("weight_scale", weight_scale), ("bias", bias_t)):
             if not t.is_cuda or not t.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous CUDA tensor")
-        if weight_scale.dtype != torch.float32 or bias_q.dtype != torch.int32:
-            raise TypeError("weight_scale must be float32 and bias_q int32")
-        if weight_scale.numel() != n or bias_q.numel() != n:
-            raise ValueError("weight_scale / bias_q must have N elements")
+        if weight_scale.dtype != torch.float32 or bias_t.dtype != (torch.float32 if per_group else torch.int32):
+            raise TypeError("weight_scale must be float32 and the bias " + ("float32" if per_group else "int32"))
+        want_scales = n * (k // 64) if per_group else n
+        if weight_scale.numel() != want_scales or bias_t.numel() != n:
+            raise ValueError(f"weight_scale must have {want_scales} elements and the bias N")
         if schema == "lpbq":
             if lpbq_block_scale is None or lpbq_block_scale.dtype != torch.uint8:
                 raise ValueError("LPBQ needs lpbq_block_scale uint8 [N, K/block]")
@@ -98,14 +109,14 @@ class QuantMatMul:
             lpbq_block_scale = lpbq_block_scale.contiguous()
         self.k, self.n = k, n
         self.device = weight.device
-        self._keep = [weight, weight_scale, bias_q, lpbq_block_scale]
+        self._keep = [weight, weight_scale, bias_t, lpbq_block_scale]
         self._w = L.QhtpMatmulWeights(
             family=L.FAMILY[family], schema=L.SCHEMA[schema], dequant=L.DEQUANT[dequant], k=k, n=n,
             lpbq_block=lpbq_block if schema == "lpbq" else 0,
-            weight=_ptr(weight), weight_scale=_ptr(weight_scale), bias_q=_ptr(bias_q),
+            weight=_ptr(weight), weight_scale=_ptr(weight_scale), bias_q=None if per_group else _ptr(bias_q),
             lpbq_block_scale=_ptr(lpbq_block_scale),
             act_scale=float(act_scale), act_offset=int(act_offset), out_scale=float(out_scale),
-            out_offset=int(out_offset))
+            out_offset=int(out_offset), bias_float=_ptr(bias_float) if per_group else None)
         self.plan = L.QhtpMatmulPlan()
         L.check("qhtp_matmul_plan", L.lib.qhtp_matmul_plan(C.byref(self._w), C.byref(self.plan)))
         with torch.cuda.device(self.device):

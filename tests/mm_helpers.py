@@ -7,7 +7,8 @@ import torch
 from oracle import mm_oracle as O
 
 KERNEL_FAMILY = {"u8i8": "u8i8", "w4a8_per_channel": "w4a8", "w4a8_lpbq": "w4a8", "w8a16": "w8a16",
-                 "w4a16_per_channel": "w4a16", "w4a16_lpbq": "w4a16", "w16a16": "w16a16"}
+                 "w4a16_per_channel": "w4a16", "w4a16_lpbq": "w4a16", "w16a16": "w16a16",
+                 "w4a8_per_group": "w4a8", "w4a16_per_group": "w4a16"}
 
 
 def to_dev(a: np.ndarray) -> torch.Tensor:
@@ -27,6 +28,10 @@ def build_op(case: O.QuantCase, dequant: str | None = None):
     kw = {}
     if fam.schema == "lpbq":
         kw = dict(schema="lpbq", lpbq_block_scale=to_dev(case.lpbq_factor), lpbq_block=fam.lpbq_block)
+    if fam.schema == "per_group":
+        return QuantMatMul(kf, w, to_dev(case.weight_scale.astype(np.float32)), None, schema="per_group",
+                           bias_float=to_dev(case.bias_float.astype(np.float32)), act_scale=case.act_scale,
+                           out_scale=case.out_scale, act_offset=case.act_offset, out_offset=case.out_offset)
     return QuantMatMul(kf, w, to_dev(case.weight_scale.astype(np.float32)), to_dev(case.bias_q.astype(np.int32)),
                        act_scale=case.act_scale, out_scale=case.out_scale, act_offset=case.act_offset,
                        out_offset=case.out_offset, dequant=dequant, **kw)

@@ -48,9 +48,10 @@ def test_generator_and_exact_model_match_reference(golden_dir, shape):
             assert O.sha256(c.lpbq_expanded) == h["lpbq_expanded_q_nk"]
         # the restated float64 formula reproduces the reference's output
         assert O.sha256(c.ref_output_q) == h["output_ref_q"]
-        if fam.schema != "per_group":
-            # the exact integer/requant model (what the GPU computes) reproduces it too
-            assert O.sha256(O.exact_output(c)) == h["output_ref_q"], (e["family"], e["case"])
+        # the model the GPU computes reproduces it too: the exact integer/requant model, or for the
+        # per-group schema the float64 sum of exact group contributions
+        got = O.per_group_output(c) if fam.schema == "per_group" else O.exact_output(c)
+        assert O.sha256(got) == h["output_ref_q"], (e["family"], e["case"])
         checked += 1
     assert checked >= 56
 
