@@ -16,8 +16,9 @@ window), max over ranks.
 
 The default line also carries the GDN C=256 inverse ("secondary", 4096 chunks) and the BASELINE
 decode/prefill rows of the W4A16 LPBQ GEMM ("decode": M in {1, 16, 128}, N in {4096, 14336}, GB/s
-against the HBM peak).  ``--workload gdn`` and ``--workload decode --m M --n N`` run one of those
-alone (the commands the committed ncu summaries were taken with).
+against the HBM peak), and the per-group W4 schema at the headline shape ("per_group": float32
+scale per 64 weights of K, float32 bias).  ``--workload gdn`` and ``--workload decode --m M --n N``
+run one of those alone (the commands the committed ncu summaries were taken with).
 """
 from __future__ import annotations
 
@@ -84,6 +85,26 @@ def synth_w4a16_lpbq(m: int, k: int, n: int, block: int, seed: int, device) -> d
     packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).t().contiguous()
     return dict(act=act, w_packed=packed, q=q, factor=f.to(torch.uint8).contiguous(), scale=scale.contiguous(),
                 bias_q=bias_q.contiguous(), s_a=s_a, s_o=s_o, m=m, k=k, n=n, block=block)
+
+
+def synth_w4a16_per_group(m: int, k: int, n: int, seed: int, device) -> dict:
+    """u16 activations as above and per-group int4 weights with the reference generator's rules:
+    symmetric float32 scale per (channel, 64 weights of K), float32 bias kept unquantized
+    (generate_qnn_matmul_python_cases.py:392-423, 460-470)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn((m, k), generator=g, device=device)
+    w = torch.randn((n, k), generator=g, device=device) * 0.02
+    b = torch.randn((n,), generator=g, device=device) * 0.1
+    s_a = max(-float(x.min()) / 32768.0, float(x.max()) / 32767.0, 1e-12)
+    act = torch.clamp(torch.round(x.double() / s_a + 32768), 0, 65535).to(torch.int32).to(torch.uint16)
+    wb = w.double().reshape(n, k // 64, 64)
+    gs = (wb.abs().amax(dim=2).clamp_min(1e-12) / 7.0).float()
+    q = torch.clamp(torch.round(wb / gs.double()[:, :, None]), -7, 7).to(torch.int8).reshape(n, k)
+    y = x[:256].double() @ w.double().t() + b.double()
+    s_o = max(-float(y.min()) / 32768.0, float(y.max()) / 32767.0, 1e-12)
+    nib = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).t().contiguous()
+    return dict(act=act, w_packed=packed, scale=gs.contiguous(), bias=b.float().contiguous(), s_a=s_a, s_o=s_o)
 
 
 def synth_gdn_A(n_chunks: int, C: int, dk: int, seed: int, device) -> torch.Tensor:
@@ -384,7 +405,37 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     if not args.no_decode:
         res["decode"] = {"workload": "W4A16 LPBQ decode/prefill rows (BASELINE configs[2])",
                          "peak_gbs": peaks()["hbm_gbs"], "rows": run_decode(args, world, rank, local, stream)}
+    if not args.no_per_group:
+        res["per_group"] = run_per_group(args, world, rank, local, stream)
     return res
+
+
+def run_per_group(args, world, rank, local, stream) -> dict:
+    """The per-group W4 schema (float32 scale per 64 weights of K) at the headline GEMM shape: the
+    same timing rules and int8 roofline denominator as the LPBQ line."""
+    from qcom_htp_b200 import QuantMatMul
+    dev = torch.device("cuda", local)
+    m, k, n = args.m, args.k, args.n
+    d = synth_w4a16_per_group(m, k, n, seed=777 + rank, device=dev)
+    op = QuantMatMul("w4a16", d["w_packed"], d["scale"], None, schema="per_group", bias_float=d["bias"],
+                     act_scale=d["s_a"], out_scale=d["s_o"])
+    act, out = d["act"], torch.empty((m, n), dtype=torch.uint16, device=dev)
+    flush = L2Flush(dev)
+    times = timed_steps(lambda: op(act, out), max(5, args.steps // 2), args.warmup, flush, world, stream)
+    op.check_device(m)
+    t = max_over_ranks(statistics.mean(times), world)
+    ops = 2.0 * m * n * k
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    achieved = ops / statistics.mean(times) / 1e12
+    return {"metric": "w4a16_per_group_gemm_tops", "value": ops * world / t / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": t * 1e3, "m": m, "k": k, "n_per_gpu": n, "group": 64,
+            "kernel": "split_u16_planes + qgemm_group_kernel<2> (channel-major, float64 group accumulation)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                         "frac": achieved / int8_peak, "executed_tflops": achieved * 4,
+                         "frac_executed": achieved * 4 / int8_peak,
+                         "note": "per 64-K group the accumulators are drained from TMEM and folded into float64"},
+            "gpu_launches": 2 * max(5, args.steps // 2)}
 
 
 def run_decode(args, world, rank, local, stream, shapes=None) -> list:
@@ -528,6 +579,7 @@ def main() -> int:
     ap.add_argument("--allgather", action="store_true")
     ap.add_argument("--no-gdn", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-per-group", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -15,8 +15,8 @@ enum GemmMode : uint32_t {
   kModeF32 = 0,    // f32 weight dequant: B tile = [q (128 ch) | e' (128 ch)], s8
   kModeExact = 1,  // exact dequant, 8-bit weights: B tile = q (128 ch), s8
   kModeW16 = 2,    // exact dequant, int16 weights: B tile = [hi s8 (128 ch) | lo u8 (128 ch)]
-  kModeGroup = 3,  // per-group W4 (float32 scale per 64 weights of K): tiles of 64 channels,
-                   // B tile = [q (64 ch) | e' (64 ch)], s8; qgroup.cu
+  kModeGroup = 3,  // per-group W4 (float32 scale per 64 weights of K): channel-major tiles,
+                   // weight image = [q (128 ch) | e' (128 ch)], s8; qgroup.cu
 };
 
 constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
@@ -24,13 +24,11 @@ constexpr int kTileN = 128;      // output channels per tile
 constexpr int kTileK = 128;      // bytes of K per pipeline stage (one 128-byte swizzle row)
 
 // weight-plane rows per tile in the prepared layout
-inline constexpr uint32_t b_rows_for_mode(uint32_t mode) {
-  return mode == kModeExact || mode == kModeGroup ? 128u : 256u;
-}
+inline constexpr uint32_t b_rows_for_mode(uint32_t mode) { return mode == kModeExact ? 128u : 256u; }
 
 // Per-group schema: channels per tile, and the constants of one (tile, group) in the prepared
-// buffer: czp int64[64] = zp*(m*sum q + sum e') | 2^e float64[64] | m int32[64]
-constexpr int kGroupTileN = 64;
+// buffer: K int64[128] = bits(1.5*2^52) - zp*(m*sum q + sum e') | 2^e float64[128] | m int32[128]
+constexpr int kGroupTileN = 128;
 constexpr int kGroupRecBytes = kGroupTileN * (8 + 8 + 4);
 inline size_t group_rec_bytes(const QhtpMatmulPlan* p) {
   const size_t b = static_cast<size_t>(p->n_tiles) * (p->k_pad / kTileK) * 2 * kGroupRecBytes;

@@ -6,24 +6,26 @@
 //     out = clip(rint(y / s_O + zp_O), 0, qmax)
 //
 // Every group scale is s[n,g] = m*2^e (m a 24-bit integer), and float32(q*s) = (q*m + e')*2^e with
-// the integer residual e' (|e'| <= 4 for int4 codes).  So one group's contribution to a row is
+// the integer residual e' (|e'| <= 8 for int4 codes).  So one group's contribution to a row is
 //
 //     Z[g] * 2^e[n,g],   Z[g] = m[n,g]*sum_g(x*q) + sum_g(x*e') - zp*(m[n,g]*sum_g q + sum_g e')
 //
-// with Z an exact int64 (|Z| < 2^50, exact in float64).  The kernel forms the two integer sums of a
-// group on the tensor cores (kind::i8: u8 activation plane x [q | e'] weight rows, one N=128 MMA per
-// plane and 32 bytes of K), drains them from TMEM after every group and accumulates
+// with Z an exact integer (|Z| < 2^50, exact in float64).  The kernel forms the two integer sums of
+// a group on the tensor cores (kind::i8), drains them from TMEM after every group and accumulates
 // acc += Z*2^e in float64, groups in K order.  The multiply by 2^e is exact, so this is the float64
 // sum of the exact group contributions; then y = s_A*acc + bias and the output rounding follow the
 // reference formula operation by operation (IEEE double, no contraction).  The oracle restates the
 // same sequence (oracle.mm_oracle.per_group_output), and that sequence reproduces the reference's
 // output_ref_q on its per-group golden cases.
 //
-// Tiles are 128 rows x 64 channels (the per-group drain holds 32 float64 accumulators per thread).
-// A 128-byte K block is one pipeline stage and two groups; the two groups' accumulators live in two
-// TMEM buffers (PA*128 columns each), so the MMAs of one group overlap the drain of the other.
+// Channel-major tiles (swap-AB): the weight images are the M = 128 operand (TMEM lane = output
+// channel) and 64 activation rows the N operand, so each epilogue thread owns one channel and reads
+// its group constants (m, 2^e, zero-point term) once per group instead of once per element.  Per
+// group and activation byte plane two MMAs (q rows, e' rows) of M=128, N=64 fill 2 x 64 TMEM columns;
+// a 128-byte K block is one pipeline stage and two groups, held in two TMEM buffers (PA*128 columns
+// each) so the MMAs of one group overlap the drain of the other.
 // Roles (384 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer, warps 2-3 idle,
-// warps 4..11 the drain/accumulate epilogue (thread = one row, 32 channels).
+// warps 4..11 the drain/accumulate epilogue (thread = one channel, 32 of the 64 rows).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -36,29 +38,34 @@ namespace qhtp {
 
 namespace {
 
-constexpr int kGroupK = 64;                   // weights per scale group (along K)
-constexpr int kGBRows = 2 * kGroupTileN;      // weight image rows per tile: [q 64 | e' 64]
+constexpr int kGroupK = 64;  // weights per scale group (along K)
+constexpr int kGRows = 64;   // activation rows per tile (the MMA N)
+// 1.5*2^52: the double whose bit pattern plus an integer Z (|Z| < 2^51) is the double 1.5*2^52 + Z
+constexpr double kMagic = 6755399441055744.0;
+constexpr int64_t kMagicBits = 0x4338000000000000ll;
+constexpr int kGWRows = 2 * kGroupTileN;        // weight image rows per tile: [q 128 | e' 128]
 constexpr int kGRecStage = 2 * kGroupRecBytes;  // the two groups of one 128-byte K block
 constexpr int kEpiW = 8, kEpiW0 = 4;
 constexpr int kThreads = 32 * (kEpiW0 + kEpiW);
 constexpr int kRegsLaunch = 168, kRegsCtrl = 40, kRegsEpi = 232;
 static_assert(kThreads * kRegsLaunch == 128 * kRegsCtrl + 32 * kEpiW * kRegsEpi, "register split");
 static_assert(kTileK == 2 * kGroupK, "a K block holds two groups");
+static_assert(kGroupTileN == 128, "one TMEM lane per channel");
 
 template <int PA>
 struct GCfg {
-  static constexpr int kStageA = kTileM * kTileK;        // 16 KB per activation plane
-  static constexpr int kStageB = kGBRows * kTileK;       // 16 KB: [q | e'] rows of 64 channels
-  static constexpr int kStage = PA * kStageA + kStageB;  // 48 KB (A16) / 32 KB (A8)
-  static constexpr int kStages = PA == 2 ? 4 : 6;
+  static constexpr int kStageW = kGWRows * kTileK;       // 32 KB: [q | e'] rows of 128 channels
+  static constexpr int kStageX = kGRows * kTileK;        // 8 KB per activation plane
+  static constexpr int kStage = kStageW + PA * kStageX;  // 48 KB (A16) / 40 KB (A8)
+  static constexpr int kStages = 4;
   static constexpr int kSmem = kStages * (kStage + kGRecStage) + 1024 + 256;
 };
 static_assert(GCfg<2>::kSmem <= 227 * 1024 && GCfg<1>::kSmem <= 227 * 1024, "shared memory");
 
 struct GroupParams {
   int M, N, m_tiles, n_tiles, kblocks, a_plane_rows;
-  const uint8_t* grec;  // [n_tiles][kblocks][2 groups][czp i64 x64 | 2^e f64 x64 | m i32 x64]
-  const double* bias;   // [n_tiles * 64] float64 of the float32 bias
+  const uint8_t* grec;  // [n_tiles][kblocks][2 groups][K i64 x128 | 2^e f64 x128 | m i32 x128]
+  const double* bias;   // [n_tiles * 128] float64 of the float32 bias
   void* out;
   double act_scale, out_scale;
   int zp_out, qmax;
@@ -76,12 +83,12 @@ __device__ __forceinline__ void regs_inc() {
 
 template <int PA>
 __global__ void __launch_bounds__(kThreads, 1)
-    qgemm_group_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    qgemm_group_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                        const GroupParams p) {
   using Cfg = GCfg<PA>;
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kBufCols = PA * 128;  // one group: per activation plane [q 64 | e' 64] columns
+  constexpr uint32_t kBufCols = PA * 128;  // one group: per activation plane [q 64 rows | e' 64 rows]
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -100,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kEpiW);  // the MMAs have read the operands, every epilogue warp the records
+      mbar_init(&empty[s], 1 + kEpiW);  // the MMAs have read the operands, every epilogue warp the constants
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -121,12 +128,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kRegsCtrl>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------------ TMA producer
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.m_tiles) * kTileM;
+        const int m0 = (tile % p.m_tiles) * kGRows;
         const int nt = tile / p.m_tiles;
         for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
           const int s = it % S;
@@ -136,17 +143,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_arrive_expect_tx(&full[s], Cfg::kStage + kGRecStage);
           uint8_t* st = stages + s * Cfg::kStage;
+          const size_t blk = static_cast<size_t>(nt) * p.kblocks + kb;
+          tma_load_2d(st, &tmW, &full[s], 0, static_cast<int>(blk * kGWRows));
 #pragma unroll
           for (int pl = 0; pl < PA; ++pl)
-            tma_load_2d(st + pl * Cfg::kStageA, &tmA, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
-          const size_t blk = static_cast<size_t>(nt) * p.kblocks + kb;
-          tma_load_2d(st + PA * Cfg::kStageA, &tmB, &full[s], 0, static_cast<int>(blk * kGBRows));
+            tma_load_2d(st + Cfg::kStageW + pl * Cfg::kStageX, &tmX, &full[s], kb * kTileK, pl * p.a_plane_rows + m0);
           bulk_load(recs + s * kGRecStage, p.grec + blk * kGRecStage, kGRecStage, &full[s]);
         }
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------------------------------------------ MMA issuer
-      constexpr uint32_t id = idesc_i8(128, kGBRows, 0, 1);  // u8 activation x s8 [q | e'] rows
+      constexpr uint32_t id = idesc_i8(128, kGRows, 1, 0);  // s8 weight rows x u8 activation rows
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -158,9 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(stages + s * Cfg::kStage);
-          const uint64_t dA0 = desc_kmajor_sw128(st);
-          const uint64_t dA1 = desc_kmajor_sw128(st + (PA > 1 ? Cfg::kStageA : 0));
-          const uint64_t dB = desc_kmajor_sw128(st + PA * Cfg::kStageA);
+          const uint64_t dQ = desc_kmajor_sw128(st);                         // q rows of 128 channels
+          const uint64_t dE = desc_kmajor_sw128(st + kGroupTileN * kTileK);  // e' rows
+          const uint64_t dX0 = desc_kmajor_sw128(st + Cfg::kStageW);
+          const uint64_t dX1 = desc_kmajor_sw128(st + Cfg::kStageW + (PA > 1 ? Cfg::kStageX : 0));
 #pragma unroll
           for (int b = 0; b < 2; ++b) {  // group 2*kb + b -> TMEM buffer b
             if (!mbar_wait(&tempty[b], (it & 1) ^ 1, p.err, kErrTimeoutOther)) {
@@ -168,11 +176,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
+            const uint32_t d = tmem + b * kBufCols;
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const uint64_t ko = static_cast<uint64_t>((2 * b + kk) * 2);  // 32 bytes, in 16-byte units
-              mma_i8(tmem + b * kBufCols, dA0 + ko, dB + ko, id, static_cast<uint32_t>(kk));
-              if constexpr (PA == 2) mma_i8(tmem + b * kBufCols + 128, dA1 + ko, dB + ko, id, static_cast<uint32_t>(kk));
+              const uint32_t accum = static_cast<uint32_t>(kk);
+              mma_i8(d + 0, dQ + ko, dX0 + ko, id, accum);   // sum x(_hi) * q
+              mma_i8(d + 64, dE + ko, dX0 + ko, id, accum);  // sum x(_hi) * e'
+              if constexpr (PA == 2) {
+                mma_i8(d + 128, dQ + ko, dX1 + ko, id, accum);  // sum x_lo * q
+                mma_i8(d + 192, dE + ko, dX1 + ko, id, accum);  // sum x_lo * e'
+              }
             }
             mma_commit(&tfull[b]);
           }
@@ -184,44 +198,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     regs_inc<kRegsEpi>();
     // ------------------------------------------------------------------ drain + float64 accumulate
-    const int quad = warp & 3;               // TMEM lane quadrant of this warp
-    const int chalf = (warp - kEpiW0) >> 2;  // channels 32*chalf .. +32 of the tile
-    const int row = quad * 32 + lane;
-    const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * 32;
+    const int quad = warp & 3;               // TMEM lane quadrant: channels 32*quad .. +32
+    const int rhalf = (warp - kEpiW0) >> 2;  // rows 32*rhalf .. +32 of the tile
+    const int ch = quad * 32 + lane;         // this thread's channel within the tile
+    const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + rhalf * 32;
     const bool u16 = p.qmax > 255;
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-      const int m = (tile % p.m_tiles) * kTileM + row;
-      const int n0 = (tile / p.m_tiles) * kGroupTileN + chalf * 32;
+      const int r0 = (tile % p.m_tiles) * kGRows + rhalf * 32;
+      const int n = (tile / p.m_tiles) * kGroupTileN + ch;
       double acc[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) acc[c] = 0.0;
+      for (int r = 0; r < 32; ++r) acc[r] = 0.0;
       for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
-        const uint8_t* rs = recs + (it % S) * kGRecStage;
+        const int s = it % S;
         // Acquire the bulk copy of the stage's group constants on its own barrier.  The phase is
         // already complete (the MMAs of this stage waited on it) and cannot advance before this
         // warp arrives on empty[], so this returns at once.
-        if (!mbar_wait(&full[it % S], (it / S) & 1, p.err, kErrTimeoutFull)) {
+        if (!mbar_wait(&full[s], (it / S) & 1, p.err, kErrTimeoutFull)) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
+          const uint8_t* rg = recs + s * kGRecStage + b * kGroupRecBytes;
+          const int64_t kz = reinterpret_cast<const int64_t*>(rg)[ch];  // bits(1.5*2^52) - zero-point term
+          const double sc = reinterpret_cast<const double*>(rg + 8 * kGroupTileN)[ch];   // 2^e
+          const int32_t mg = reinterpret_cast<const int32_t*>(rg + 16 * kGroupTileN)[ch];  // m
           if (!mbar_wait(&tfull[b], it & 1, p.err, kErrTimeoutAccum)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint8_t* rg = rs + b * kGroupRecBytes;
-          const int64_t* czp = reinterpret_cast<const int64_t*>(rg) + chalf * 32;
-          const double* sc = reinterpret_cast<const double*>(rg + 512) + chalf * 32;
-          const int32_t* mg = reinterpret_cast<const int32_t*>(rg + 1024) + chalf * 32;
           const uint32_t tb = tl + b * kBufCols;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t qh[16], eh[16], ql[16], el[16];
-            tmem_ld16(tb + h * 16, qh);       // sum x(_hi) * q
+            tmem_ld16(tb + h * 16, qh);       // sum x(_hi) * q, rows 16h..
             tmem_ld16(tb + 64 + h * 16, eh);  // sum x(_hi) * e'
             if constexpr (PA == 2) {
               tmem_ld16(tb + 128 + h * 16, ql);  // sum x_lo * q
@@ -235,7 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const int c = h * 16 + j;
               int32_t pq, pe;
               if constexpr (PA == 2) {
                 pq = static_cast<int32_t>(qh[j]) * 256 + static_cast<int32_t>(ql[j]);  // |.| < 2^26
@@ -244,43 +257,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pq = static_cast<int32_t>(qh[j]);
                 pe = static_cast<int32_t>(eh[j]);
               }
-              const int64_t z = static_cast<int64_t>(mg[c]) * pq + pe - czp[c];  // exact, |z| < 2^50
-              acc[c] = __fma_rn(static_cast<double>(z), sc[c], acc[c]);          // z*2^e exact: one rounding
+              // bits of the double 1.5*2^52 + Z; exact for |Z| < 2^51, and |Z| < 2^50 here
+              const int64_t t = static_cast<int64_t>(mg) * pq + (kz + pe);
+              const double z = __dsub_rn(__longlong_as_double(t), kMagic);  // Z, exact
+              acc[h * 16 + j] = __fma_rn(z, sc, acc[h * 16 + j]);          // Z*2^e exact: one rounding
             }
           }
         }
         if (!ok) break;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[it % S]);  // this warp is done with the stage's group records
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's group constants
       }
       if (!ok) break;
-      if (m < p.M && n0 < p.N) {
-        uint32_t code[32];
+      if (n < p.N) {
+        const double bias = __ldg(p.bias + n);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const double y = __dadd_rn(__dmul_rn(p.act_scale, acc[c]), __ldg(p.bias + n0 + c));
-          double z = rint(__dadd_rn(__ddiv_rn(y, p.out_scale), static_cast<double>(p.zp_out)));
-          z = fmin(fmax(z, 0.0), static_cast<double>(p.qmax));
-          code[c] = static_cast<uint32_t>(z);
-        }
-        if (u16) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n0);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint32_t* cd = code + 8 * v;
-            dst[v] = make_uint4(cd[0] | (cd[1] << 16), cd[2] | (cd[3] << 16), cd[4] | (cd[5] << 16),
-                                cd[6] | (cd[7] << 16));
-          }
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n0);
-#pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            const uint32_t* cd = code + 16 * v;
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              w[i] = cd[4 * i] | (cd[4 * i + 1] << 8) | (cd[4 * i + 2] << 16) | (cd[4 * i + 3] << 24);
-            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int r = 0; r < 32; ++r) {  // fully unrolled: acc[] stays in registers
+          if (r0 + r < p.M) {
+            const double y = __dadd_rn(__dmul_rn(p.act_scale, acc[r]), bias);
+            double z = rint(__dadd_rn(__ddiv_rn(y, p.out_scale), static_cast<double>(p.zp_out)));
+            z = fmin(fmax(z, 0.0), static_cast<double>(p.qmax));
+            const size_t o = static_cast<size_t>(r0 + r) * p.N + n;  // a warp: 32 consecutive channels
+            if (u16)
+              reinterpret_cast<uint16_t*>(p.out)[o] = static_cast<uint16_t>(z);
+            else
+              reinterpret_cast<uint8_t*>(p.out)[o] = static_cast<uint8_t>(z);
           }
         }
       }
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int PA>
-cudaError_t launch_group_variant(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
+cudaError_t launch_group_variant(cudaStream_t stream, const CUtensorMap& tx, const CUtensorMap& tw,
                                  const GroupParams& prm, int sms) {
   using Cfg = GCfg<PA>;
   static bool attr_done = false;
@@ -307,13 +308,13 @@ cudaError_t launch_group_variant(cudaStream_t stream, const CUtensorMap& ta, con
   }
   const int total = prm.m_tiles * prm.n_tiles;
   const int grid = total < sms ? total : sms;
-  qgemm_group_kernel<PA><<<grid, kThreads, Cfg::kSmem, stream>>>(ta, tb, prm);
+  qgemm_group_kernel<PA><<<grid, kThreads, Cfg::kSmem, stream>>>(tx, tw, prm);
   return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------------
 // Prepare: one thread per (channel, group).  Writes the group's 64 q and 64 e' bytes into the
-// pre-swizzled operand image of its (tile, K block) and the group's constants into the record block.
+// pre-swizzled operand image of its (tile, K block) and the group's constants into its block.
 // ------------------------------------------------------------------------------------------------
 __global__ void prepare_group_kernel(const uint8_t* __restrict__ w4, const float* __restrict__ scale,
                                      const float* __restrict__ bias, uint32_t K, uint32_t N, uint32_t kblocks,
@@ -329,20 +330,21 @@ __global__ void prepare_group_kernel(const uint8_t* __restrict__ w4, const float
     const uint32_t tile = n / kGroupTileN, rr = n % kGroupTileN, kb = g / 2, half = g % 2;
     const size_t blk = static_cast<size_t>(tile) * kblocks + kb;
     uint8_t* rg = grec + blk * kGRecStage + half * kGroupRecBytes;
+    if (g == 0) bias_d[n] = static_cast<double>(bias[n]);
     if ((bits >> 31) != 0 || ex == 0 || ex == 0xFF) {  // negative, zero/subnormal, inf/nan
       atomicCAS(bad_scale, 0, 1);
       continue;
     }
     const int32_t ms = static_cast<int32_t>((bits & 0x7FFFFFu) | 0x800000u);
     const int es = static_cast<int>(ex) - 150;  // scale = ms * 2^es
-    int8_t* img = planes + blk * (kGBRows * kTileK);
+    int8_t* img = planes + blk * (kGWRows * kTileK);
     long long sq = 0, se = 0;
 #pragma unroll 1
     for (uint32_t c4 = 0; c4 < 4; ++c4) {
       const uint32_t k0 = g * kGroupK + c4 * 16;
       const uint32_t c = half * 4 + c4;  // 16-byte chunk of the 128-byte K row
       int8_t* rq = img + rr * kTileK + (((c ^ rr) & 7u) << 4);
-      int8_t* re = img + (kGroupTileN + rr) * kTileK + (((c ^ rr) & 7u) << 4);  // row 64+rr: same swizzle phase
+      int8_t* re = img + (kGroupTileN + rr) * kTileK + (((c ^ rr) & 7u) << 4);  // row 128+rr: same swizzle phase
 #pragma unroll 4
       for (int j = 0; j < 16; ++j) {
         const uint32_t k = k0 + j;
@@ -358,10 +360,10 @@ __global__ void prepare_group_kernel(const uint8_t* __restrict__ w4, const float
         se += e;
       }
     }
-    reinterpret_cast<int64_t*>(rg)[rr] = static_cast<int64_t>(act_zp) * (static_cast<int64_t>(ms) * sq + se);
-    reinterpret_cast<double*>(rg + 512)[rr] = ldexp(1.0, es);
-    reinterpret_cast<int32_t*>(rg + 1024)[rr] = ms;
-    if (g == 0) bias_d[n] = static_cast<double>(bias[n]);
+    reinterpret_cast<int64_t*>(rg)[rr] =
+        kMagicBits - static_cast<int64_t>(act_zp) * (static_cast<int64_t>(ms) * sq + se);
+    reinterpret_cast<double*>(rg + 8 * kGroupTileN)[rr] = ldexp(1.0, es);
+    reinterpret_cast<int32_t*>(rg + 16 * kGroupTileN)[rr] = ms;
   }
 }
 
@@ -386,18 +388,18 @@ cudaError_t launch_prepare_group(const QhtpMatmulPlan* plan, const QhtpMatmulWei
 
 cudaError_t launch_gemm_group(const GemmLaunch& g, const uint8_t* a_base, uint64_t a_rows, int sms) {
   const QhtpMatmulPlan* pl = g.plan;
-  CUtensorMap ta, tb;
-  if (!make_tmap_2d_u8(&ta, a_base, pl->k, a_rows, pl->k, kTileK, kTileM)) return cudaErrorInvalidValue;
+  CUtensorMap tx, tw;
+  if (!make_tmap_2d_u8(&tx, a_base, pl->k, a_rows, pl->k, kTileK, kGRows)) return cudaErrorInvalidValue;
   const uint32_t kblocks = pl->k_pad / kTileK;
-  const uint64_t brows = static_cast<uint64_t>(pl->n_tiles) * kblocks * kGBRows;
-  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl->prepared, kTileK, brows, kTileK, kTileK, kGBRows,
+  const uint64_t wrows = static_cast<uint64_t>(pl->n_tiles) * kblocks * kGWRows;
+  if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl->prepared, kTileK, wrows, kTileK, kTileK, kGWRows,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   const uint8_t* base = static_cast<const uint8_t*>(pl->prepared);
   GroupParams prm;
   prm.M = static_cast<int>(g.m);
   prm.N = static_cast<int>(pl->n);
-  prm.m_tiles = static_cast<int>((g.m + kTileM - 1) / kTileM);
+  prm.m_tiles = static_cast<int>((g.m + kGRows - 1) / kGRows);
   prm.n_tiles = static_cast<int>(pl->n_tiles);
   prm.kblocks = static_cast<int>(kblocks);
   prm.a_plane_rows = static_cast<int>(g.m);
@@ -409,8 +411,8 @@ cudaError_t launch_gemm_group(const GemmLaunch& g, const uint8_t* a_base, uint64
   prm.zp_out = pl->out_zp;
   prm.qmax = pl->out_qmax;
   prm.err = g.err;
-  return pl->a_planes == 2 ? launch_group_variant<2>(g.stream, ta, tb, prm, sms)
-                           : launch_group_variant<1>(g.stream, ta, tb, prm, sms);
+  return pl->a_planes == 2 ? launch_group_variant<2>(g.stream, tx, tw, prm, sms)
+                           : launch_group_variant<1>(g.stream, tx, tw, prm, sms);
 }
 
 }  // namespace qhtp

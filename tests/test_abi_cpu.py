@@ -67,15 +67,15 @@ def test_plan_rejects(L, kw, status):
 
 
 def test_plan_per_group(L):
-    """Per-group W4 schema (generate_qnn_matmul_python_cases.py:392-423): 64-channel tiles, 128 weight
+    """Per-group W4 schema (generate_qnn_matmul_python_cases.py:392-423): 128-channel tiles, 256 weight
     rows ([q | e']) per tile, K a multiple of 64 above 64, float32-dequant only, W4 families only."""
     p = L.QhtpMatmulPlan()
     w = _weights(L, schema=L.SCHEMA["per_group"], lpbq_block=0, bias_q=None, bias_float=1, lpbq_block_scale=None,
                  k=4096 + 64, n=14336 + 32)
     assert L.lib.qhtp_matmul_plan(C.byref(w), C.byref(p)) == L.OK
-    assert p.mode == 3 and p.ch_per_tile == 64 and p.n_tiles == 225 and p.k_pad == 4224
-    # planes (128 rows x k_pad per tile) + group constants (1280 bytes per tile and group) + bias
-    assert p.prepared_bytes >= 225 * 128 * 4224 + 225 * 66 * 1280 + 225 * 64 * 8
+    assert p.mode == 3 and p.ch_per_tile == 128 and p.n_tiles == 113 and p.k_pad == 4224
+    # planes (256 rows x k_pad per tile) + group constants (2560 bytes per tile and group) + bias
+    assert p.prepared_bytes >= 113 * 256 * 4224 + 113 * 66 * 2560 + 113 * 128 * 8
     for kw, status in [(dict(k=64), 2), (dict(k=96), 2), (dict(family=L.FAMILY["w8a16"]), 2),
                        (dict(family=L.FAMILY["u8i8"]), 2), (dict(dequant=1), 2)]:
         ww = _weights(L, schema=L.SCHEMA["per_group"], lpbq_block=0, bias_float=1, **kw)
