@@ -22,10 +22,11 @@
 // channel) and 64 activation rows the N operand, so each epilogue thread owns one channel and reads
 // its group constants (m, 2^e, zero-point term) once per group instead of once per element.  Per
 // group and activation byte plane two MMAs (q rows, e' rows) of M=128, N=64 fill 2 x 64 TMEM columns;
-// a 128-byte K block is one pipeline stage and two groups, held in two TMEM buffers (PA*128 columns
-// each) so the MMAs of one group overlap the drain of the other.
-// Roles (384 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer, warps 2-3 idle,
-// warps 4..11 the drain/accumulate epilogue (thread = one channel, 32 of the 64 rows).
+// a 128-byte K block is one pipeline stage and two groups; groups rotate through 512 / (PA*128) TMEM
+// buffers (2 for u16 activations, 4 for u8) so the MMAs of later groups overlap the drain of one.
+// Roles (640 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer, warps 2-3 idle,
+// warps 4..19 the drain/accumulate epilogue (thread = one channel, 16 of the 64 rows; four warps per
+// TMEM lane quadrant, four per scheduler, which hides the TMEM-load and float64 latencies).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -45,10 +46,8 @@ constexpr double kMagic = 6755399441055744.0;
 constexpr int64_t kMagicBits = 0x4338000000000000ll;
 constexpr int kGWRows = 2 * kGroupTileN;        // weight image rows per tile: [q 128 | e' 128]
 constexpr int kGRecStage = 2 * kGroupRecBytes;  // the two groups of one 128-byte K block
-constexpr int kEpiW = 8, kEpiW0 = 4;
+constexpr int kEpiW = 16, kEpiW0 = 4;  // 16 drain warps: four per scheduler hide the TMEM-load latency
 constexpr int kThreads = 32 * (kEpiW0 + kEpiW);
-constexpr int kRegsLaunch = 168, kRegsCtrl = 40, kRegsEpi = 232;
-static_assert(kThreads * kRegsLaunch == 128 * kRegsCtrl + 32 * kEpiW * kRegsEpi, "register split");
 static_assert(kTileK == 2 * kGroupK, "a K block holds two groups");
 static_assert(kGroupTileN == 128, "one TMEM lane per channel");
 
@@ -72,13 +71,10 @@ struct GroupParams {
   int* err;
 };
 
-template <int N>
-__device__ __forceinline__ void regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+__device__ __forceinline__ void tmem_ld8_g(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 
 template <int PA>
@@ -89,6 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kBufCols = PA * 128;  // one group: per activation plane [q 64 rows | e' 64 rows]
+  constexpr uint32_t NB = kTmemCols / kBufCols;  // group buffers in TMEM: 2 (A16), 4 (A8)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -96,9 +93,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* recs = smem + S * Cfg::kStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(recs + S * kGRecStage);
   uint64_t* empty = full + S;
-  uint64_t* tfull = empty + S;   // [2]: group buffer b holds accumulators
-  uint64_t* tempty = tfull + 2;  // [2]: group buffer b drained
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tfull = empty + S;    // [NB]: group buffer holds accumulators
+  uint64_t* tempty = tfull + NB;  // [NB]: group buffer drained
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + NB);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -109,7 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1 + kEpiW);  // the MMAs have read the operands, every epilogue warp the constants
     }
-    for (int b = 0; b < 2; ++b) {
+    for (uint32_t b = 0; b < NB; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiW);
     }
@@ -125,7 +122,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tslot;
 
   if (warp < kEpiW0) {
-    regs_dec<kRegsCtrl>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------------ TMA producer
       tma_prefetch_desc(&tmX);
@@ -171,12 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t dX1 = desc_kmajor_sw128(st + Cfg::kStageW + (PA > 1 ? Cfg::kStageX : 0));
 #pragma unroll
           for (int b = 0; b < 2; ++b) {  // group 2*kb + b -> TMEM buffer b
-            if (!mbar_wait(&tempty[b], (it & 1) ^ 1, p.err, kErrTimeoutOther)) {
+            const uint32_t gi = 2 * it + b, bf = gi % NB;  // group counter -> TMEM buffer
+            if (!mbar_wait(&tempty[bf], ((gi / NB) & 1) ^ 1, p.err, kErrTimeoutOther)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t d = tmem + b * kBufCols;
+            const uint32_t d = tmem + bf * kBufCols;
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const uint64_t ko = static_cast<uint64_t>((2 * b + kk) * 2);  // 32 bytes, in 16-byte units
@@ -188,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_i8(d + 192, dE + ko, dX1 + ko, id, accum);  // sum x_lo * e'
               }
             }
-            mma_commit(&tfull[b]);
+            mma_commit(&tfull[bf]);
           }
           if (!ok) break;
           mma_commit(&empty[s]);  // operands read
@@ -196,21 +193,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    regs_inc<kRegsEpi>();
     // ------------------------------------------------------------------ drain + float64 accumulate
-    const int quad = warp & 3;               // TMEM lane quadrant: channels 32*quad .. +32
-    const int rhalf = (warp - kEpiW0) >> 2;  // rows 32*rhalf .. +32 of the tile
-    const int ch = quad * 32 + lane;         // this thread's channel within the tile
-    const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + rhalf * 32;
+    const int quad = warp & 3;                 // TMEM lane quadrant: channels 32*quad .. +32
+    const int rquart = (warp - kEpiW0) >> 2;   // rows 16*rquart .. +16 of the tile
+    const int ch = quad * 32 + lane;           // this thread's channel within the tile
+    const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + rquart * 16;
     const bool u16 = p.qmax > 255;
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-      const int r0 = (tile % p.m_tiles) * kGRows + rhalf * 32;
+      const int r0 = (tile % p.m_tiles) * kGRows + rquart * 16;
       const int n = (tile / p.m_tiles) * kGroupTileN + ch;
-      double acc[32];
+      double acc[16];
 #pragma unroll
-      for (int r = 0; r < 32; ++r) acc[r] = 0.0;
+      for (int r = 0; r < 16; ++r) acc[r] = 0.0;
       for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
         const int s = it % S;
         // Acquire the bulk copy of the stage's group constants on its own barrier.  The phase is
@@ -226,29 +222,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t kz = reinterpret_cast<const int64_t*>(rg)[ch];  // bits(1.5*2^52) - zero-point term
           const double sc = reinterpret_cast<const double*>(rg + 8 * kGroupTileN)[ch];   // 2^e
           const int32_t mg = reinterpret_cast<const int32_t*>(rg + 16 * kGroupTileN)[ch];  // m
-          if (!mbar_wait(&tfull[b], it & 1, p.err, kErrTimeoutAccum)) {
+          const uint32_t gi = 2 * it + b, bf = gi % NB;  // group counter -> TMEM buffer
+          if (!mbar_wait(&tfull[bf], (gi / NB) & 1, p.err, kErrTimeoutAccum)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t tb = tl + b * kBufCols;
+          const uint32_t tb = tl + bf * kBufCols;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            uint32_t qh[16], eh[16], ql[16], el[16];
-            tmem_ld16(tb + h * 16, qh);       // sum x(_hi) * q, rows 16h..
-            tmem_ld16(tb + 64 + h * 16, eh);  // sum x(_hi) * e'
+            uint32_t qh[8], eh[8], ql[8], el[8];
+            tmem_ld8_g(tb + h * 8, qh);       // sum x(_hi) * q, rows 8h..
+            tmem_ld8_g(tb + 64 + h * 8, eh);  // sum x(_hi) * e'
             if constexpr (PA == 2) {
-              tmem_ld16(tb + 128 + h * 16, ql);  // sum x_lo * q
-              tmem_ld16(tb + 192 + h * 16, el);  // sum x_lo * e'
+              tmem_ld8_g(tb + 128 + h * 8, ql);  // sum x_lo * q
+              tmem_ld8_g(tb + 192 + h * 8, el);  // sum x_lo * e'
             }
             tmem_ld_wait();
             if (h == 1) {  // buffer b fully in registers: the next group's MMAs may overwrite it
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(&tempty[b]);
+              if (lane == 0) mbar_arrive(&tempty[bf]);
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < 8; ++j) {
               int32_t pq, pe;
               if constexpr (PA == 2) {
                 pq = static_cast<int32_t>(qh[j]) * 256 + static_cast<int32_t>(ql[j]);  // |.| < 2^26
@@ -260,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // bits of the double 1.5*2^52 + Z; exact for |Z| < 2^51, and |Z| < 2^50 here
               const int64_t t = static_cast<int64_t>(mg) * pq + (kz + pe);
               const double z = __dsub_rn(__longlong_as_double(t), kMagic);  // Z, exact
-              acc[h * 16 + j] = __fma_rn(z, sc, acc[h * 16 + j]);          // Z*2^e exact: one rounding
+              acc[h * 8 + j] = __fma_rn(z, sc, acc[h * 8 + j]);            // Z*2^e exact: one rounding
             }
           }
         }
@@ -272,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n < p.N) {
         const double bias = __ldg(p.bias + n);
 #pragma unroll
-        for (int r = 0; r < 32; ++r) {  // fully unrolled: acc[] stays in registers
+        for (int r = 0; r < 16; ++r) {  // fully unrolled: acc[] stays in registers
           if (r0 + r < p.M) {
             const double y = __dadd_rn(__dmul_rn(p.act_scale, acc[r]), bias);
             double z = rint(__dadd_rn(__ddiv_rn(y, p.out_scale), static_cast<double>(p.zp_out)));
