@@ -17,8 +17,9 @@ window), max over ranks.
 The default line also carries the GDN C=256 inverse ("secondary", 4096 chunks) and the BASELINE
 decode/prefill rows of the W4A16 LPBQ GEMM ("decode": M in {1, 16, 128}, N in {4096, 14336}, GB/s
 against the HBM peak), and the per-group W4 schema at the headline shape ("per_group": float32
-scale per 64 weights of K, float32 bias).  ``--workload gdn`` and ``--workload decode --m M --n N``
-run one of those alone (the commands the committed ncu summaries were taken with).
+scale per 64 weights of K, float32 bias).  ``--workload gdn``, ``--workload decode --m M --n N`` and
+``--workload per_group --m M --n N`` run one of those alone (the commands the committed ncu
+summaries were taken with).
 """
 from __future__ import annotations
 
@@ -571,7 +572,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gdn", "decode"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "gdn", "decode", "per_group"], default="gemm")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--n", type=int, default=14336)
@@ -595,6 +596,17 @@ def main() -> int:
         res = run_gemm(args, world, rank, local, stream)
     elif args.workload == "gdn":
         res = run_gdn(args, world, rank, local, stream)
+    elif args.workload == "per_group":
+        # the per-group W4A16 GEMM alone at --m / --k / --n (the command its ncu summary was taken with)
+        row = run_per_group(args, world, rank, local, stream)
+        res = {"metric": row["metric"], "value": row["value"], "unit": row["unit"], "n_gpus": world,
+               "steps": max(5, args.steps // 2), "warmup": args.warmup, "ms_per_step": row["ms_per_step"],
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "dtype": "u16xint4->u16 (int8 tensor ops, float64 group fold)",
+               "data": "synthetic (BASELINE.json distributions, generated on device)",
+               "config": {"workload": f"W4A16 per-group GEMM {args.m}x{args.k}x{args.n}", "m": args.m, "k": args.k,
+                          "n": args.n, "group": 64, "l2": "flushed between steps (256 MB write + 256 MB read)"},
+               "roofline": row["roofline"], "gpu_launches": row["gpu_launches"], "e2e": None}
     else:
         # one decode-shaped GEMM (the --m / --n shape, K = 4096), HBM roofline
         row = run_decode(args, world, rank, local, stream, shapes=[(args.m, args.n)])[0]

@@ -12,6 +12,10 @@ output, and turns a non-OK status into ``QhtpError`` (a ``RuntimeError``) carryi
         carriers of ``QuantMatMul``; ``lpbq_block_scale`` None (per-channel) or uint8 [N, K/block].
         The prepared weights (qhtp_matmul_prepare) are cached per weight tensors and parameters,
         and rebuilt when a weight tensor is modified in place.
+    torch.ops.qhtp.matmul_per_group_<family>(act, weight, weight_scale, bias_float, act_scale, act_offset,
+                                             out_scale, out_offset) -> out
+        family in w4a8, w4a16: the per-group W4 schema (generate_qnn_matmul_python_cases.py:392-423):
+        weight_scale float32 [N, K/64], bias_float float32 [N]; prepared weights cached like the above.
     torch.ops.qhtp.gdn_inverse(A bf16 [..., C, C]) -> T float32
     torch.ops.qhtp.gdn_chunk_inverse(k bf16 [..., 256, 128], beta, g float32 [..., 256]) -> T float32
     torch.ops.qhtp.gdn_solve_u16(A uint16 [..., C, C], zpA, sA, zpT, sT) -> T uint16
@@ -75,6 +79,34 @@ def _register_matmul(family: str) -> None:
 
 for _family in FAMILY_BITS:
     _register_matmul(_family)
+
+
+def _register_matmul_per_group(family: str) -> None:
+    out_dtype = torch.uint16 if FAMILY_BITS[family][2] == 16 else torch.uint8
+
+    @torch.library.custom_op(f"qhtp::matmul_per_group_{family}", mutates_args=(), device_types="cuda")
+    def _op(act: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor, bias_float: torch.Tensor,
+            act_scale: float, act_offset: int, out_scale: float, out_offset: int) -> torch.Tensor:
+        key = ("per_group", family, _key(weight), _key(weight_scale), _key(bias_float), act_scale, act_offset,
+               out_scale, out_offset)
+        op = _CACHE.get(key)
+        if op is None:
+            op = QuantMatMul(family, weight, weight_scale, None, schema="per_group", bias_float=bias_float,
+                             act_scale=act_scale, out_scale=out_scale, act_offset=act_offset, out_offset=out_offset)
+            _CACHE[key] = op
+            while len(_CACHE) > _CACHE_SIZE:
+                _CACHE.popitem(last=False)
+        else:
+            _CACHE.move_to_end(key)
+        return op(act.contiguous())
+
+    @_op.register_fake
+    def _(act, weight, weight_scale, bias_float, act_scale, act_offset, out_scale, out_offset):
+        return act.new_empty((act.shape[0], weight.shape[1]), dtype=out_dtype)
+
+
+for _family in ("w4a8", "w4a16"):
+    _register_matmul_per_group(_family)
 
 
 @torch.library.custom_op("qhtp::gdn_inverse", mutates_args=(), device_types="cuda")

@@ -6,6 +6,7 @@ from torch._subclasses.fake_tensor import FakeTensorMode
 import qcom_htp_b200  # noqa: F401  (registers the ops)
 
 OPS = ["matmul_u8i8", "matmul_w4a8", "matmul_w8a16", "matmul_w4a16", "matmul_w16a16",
+       "matmul_per_group_w4a8", "matmul_per_group_w4a16",
        "gdn_inverse", "gdn_chunk_inverse", "gdn_solve_u16"]
 
 
@@ -31,6 +32,12 @@ def test_fake_shapes():
         out = torch.ops.qhtp.matmul_w16a16(a16, torch.empty((96, 64), dtype=torch.int16, device=d), f32(96),
                                            i32(96), None, 0, 0.1, -32768, 0.2, -32768)
         assert out.shape == (5, 96) and out.dtype == torch.uint16
+        out = torch.ops.qhtp.matmul_per_group_w4a16(a16, torch.empty((32, 96), dtype=torch.uint8, device=d),
+                                                    f32(96, 1), f32(96), 0.1, -32768, 0.2, -32768)
+        assert out.shape == (5, 96) and out.dtype == torch.uint16
+        out = torch.ops.qhtp.matmul_per_group_w4a8(a8, torch.empty((32, 96), dtype=torch.uint8, device=d),
+                                                   f32(96, 1), f32(96), 0.1, -128, 0.2, 0)
+        assert out.shape == (5, 96) and out.dtype == torch.uint8
         A = torch.empty((3, 256, 256), dtype=torch.bfloat16, device=d)
         assert torch.ops.qhtp.gdn_inverse(A).dtype == torch.float32
         Ac = torch.empty((3, 64, 64), dtype=torch.uint16, device=d)

@@ -1,4 +1,4 @@
-"""torch.ops.qhtp.* on the GPU: the matmul ops give the oracle's bytes (per-channel and LPBQ), reuse
+"""torch.ops.qhtp.* on the GPU: the matmul ops give the oracle's bytes (per-channel, LPBQ, per-group), reuse
 their prepared weights across calls and re-prepare when a weight tensor changes in place, and the
 GDN ops match the direct wrappers; a bad argument surfaces as QhtpError (a RuntimeError)."""
 import numpy as np
@@ -34,6 +34,24 @@ def test_matmul_op_bit_exact_and_cached(family, op):
     torch.cuda.synchronize()
     assert len(ops._CACHE) == n_cached                     # the second call reused the prepared weights
     np.testing.assert_array_equal(out1.cpu().numpy(), O.exact_output(c))
+    assert torch.equal(out1, out2)
+
+
+@pytest.mark.parametrize("family", ["w4a8_per_group", "w4a16_per_group"])
+def test_per_group_op_bit_exact_and_cached(family):
+    """torch.ops.qhtp.matmul_per_group_<family>: the oracle's codes, prepared weights reused."""
+    import qcom_htp_b200.ops as ops
+    c = O.generate_case(family, "normal_random", 80, 320, 192)
+    args = (to_dev(O.pack_int4_kpair(c.weight_q)), to_dev(c.weight_scale.astype(np.float32)),
+            to_dev(c.bias_float.astype(np.float32)), float(c.act_scale), int(c.act_offset), float(c.out_scale),
+            int(c.out_offset))
+    fn = getattr(torch.ops.qhtp, "matmul_per_group_" + family.split("_")[0])
+    out1 = fn(to_dev(c.act_q), *args)
+    n_cached = len(ops._CACHE)
+    out2 = fn(to_dev(c.act_q), *args)
+    torch.cuda.synchronize()
+    assert len(ops._CACHE) == n_cached
+    np.testing.assert_array_equal(out1.cpu().numpy(), O.per_group_output(c))
     assert torch.equal(out1, out2)
 
 
