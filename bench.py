@@ -105,7 +105,8 @@ def synth_w4a16_per_group(m: int, k: int, n: int, seed: int, device) -> dict:
     s_o = max(-float(y.min()) / 32768.0, float(y.max()) / 32767.0, 1e-12)
     nib = (q.to(torch.int16) & 0xF).to(torch.uint8)
     packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).t().contiguous()
-    return dict(act=act, w_packed=packed, scale=gs.contiguous(), bias=b.float().contiguous(), s_a=s_a, s_o=s_o)
+    return dict(act=act, w_packed=packed, q=q, scale=gs.contiguous(), bias=b.float().contiguous(), s_a=s_a,
+                s_o=s_o, k=k, n=n)
 
 
 def synth_gdn_A(n_chunks: int, C: int, dk: int, seed: int, device) -> torch.Tensor:
@@ -305,6 +306,40 @@ def cpu_gemm_baseline(d: dict, budget_s: float = 12.0) -> dict:
             "seconds": elapsed}
 
 
+def cpu_per_group_baseline(d: dict, budget_s: float = 8.0) -> dict:
+    """The reference's float64 path for the per-group schema on a row sample:
+    y = x_deq @ w_deq.T + bias with w_deq = float32(q * s[n, k/64]) (generate_qnn_matmul_python_cases.py
+    :392-423, 460-481), then the affine requant."""
+    from oracle import mm_oracle as O   # the checker; timed here as the reference CPU implementation
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"),
+                      default=os.cpu_count())
+    except Exception:
+        threads = os.cpu_count()
+    k, n = d["k"], d["n"]
+    q = d["q"].cpu().numpy()
+    scale = d["scale"].cpu().numpy()
+    w_deq = (q.astype(np.float32) * np.repeat(scale, 64, axis=1)).astype(np.float64)   # prepared once
+    bias = d["bias"].cpu().numpy().astype(np.float64)
+    act = d["act"].cpu().numpy()
+    rows, elapsed = 8, 0.0
+    while True:
+        xs = act[:rows]
+        t0 = time.perf_counter()
+        x_deq = (xs.astype(np.float64) - 32768) * d["s_a"]
+        y = x_deq @ w_deq.T + bias
+        O.quantize_affine(y, d["s_o"], -32768, 65535, np.uint16)
+        elapsed = time.perf_counter() - t0
+        if elapsed * 2 > budget_s or rows * 2 > act.shape[0]:
+            break
+        rows *= 2
+    return {"value": 2.0 * rows * n * k / elapsed / 1e12, "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
+            "sample": f"{rows} of {act.shape[0]} rows, full K={k}, N={n}: float64 x_deq @ w_deq.T + bias, "
+                      f"requant (generate_qnn_matmul_python_cases.py:460-481 restated); {elapsed:.2f} s",
+            "seconds": elapsed}
+
+
 def cpu_gdn_baseline(A: torch.Tensor, budget_s: float = 10.0) -> dict:
     from oracle import gdn_oracle as G
     import ctypes
@@ -429,7 +464,7 @@ def run_per_group(args, world, rank, local, stream) -> dict:
     pk = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]
     achieved = ops / statistics.mean(times) / 1e12
-    return {"metric": "w4a16_per_group_gemm_tops", "value": ops * world / t / 1e12, "unit": "TFLOP/s",
+    res = {"metric": "w4a16_per_group_gemm_tops", "value": ops * world / t / 1e12, "unit": "TFLOP/s",
             "ms_per_step": t * 1e3, "m": m, "k": k, "n_per_gpu": n, "group": 64,
             "kernel": "split_u16_planes + qgemm_group_kernel<2> (channel-major, float64 group accumulation)",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
@@ -437,6 +472,9 @@ def run_per_group(args, world, rank, local, stream) -> dict:
                          "frac_executed": achieved * 4 / int8_peak,
                          "note": "per 64-K group the accumulators are drained from TMEM and folded into float64"},
             "gpu_launches": 2 * max(5, args.steps // 2)}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_per_group_baseline(d)
+    return res
 
 
 def run_decode(args, world, rank, local, stream, shapes=None) -> list:
@@ -607,6 +645,8 @@ def main() -> int:
                "config": {"workload": f"W4A16 per-group GEMM {args.m}x{args.k}x{args.n}", "m": args.m, "k": args.k,
                           "n": args.n, "group": 64, "l2": "flushed between steps (256 MB write + 256 MB read)"},
                "roofline": row["roofline"], "gpu_launches": row["gpu_launches"], "e2e": None}
+        if "cpu_baseline" in row:
+            res["cpu_baseline"] = row["cpu_baseline"]
     else:
         # one decode-shaped GEMM (the --m / --n shape, K = 4096), HBM roofline
         row = run_decode(args, world, rank, local, stream, shapes=[(args.m, args.n)])[0]

@@ -55,3 +55,30 @@ def test_bad_group_scale_rejected():
     c.weight_scale[3, 1] = 0.0
     with pytest.raises(QhtpError):
         build_op(c)
+
+
+def test_chain_per_group():
+    """CHAIN mode (each output feeds the next activation, K == N) with per-group weights."""
+    import dataclasses
+
+    import torch
+    c = O.generate_case("w4a16_per_group", "normal_random", 64, 256, 256)
+    op = build_op(c)
+    out = torch.empty((64, 256), dtype=torch.uint16, device="cuda")
+    op.run_prepared(to_dev(c.act_q), out, chain=3)
+    x = c.act_q
+    for _ in range(3):
+        x = O.per_group_output(dataclasses.replace(c, act_q=x))
+    np.testing.assert_array_equal(out.cpu().numpy(), x)
+
+
+def test_host_buffers_per_group():
+    """qhtp_matmul_run_host (pinned host activation and output, row chunks) with per-group weights."""
+    import torch
+    c = O.generate_case("w4a8_per_group", "scale_only", 300, 256, 192)
+    op = build_op(c)
+    act_h = torch.from_numpy(np.ascontiguousarray(c.act_q)).pin_memory()
+    out_h = op.run_host(act_h, chunk_rows=128)
+    torch.cuda.synchronize()
+    op.check_host()
+    np.testing.assert_array_equal(out_h.numpy(), O.per_group_output(c))
