@@ -568,6 +568,15 @@ def run_gdn(args, world, rank, local, stream, secondary=False) -> dict:
                       "note": "k bf16 [C,128], beta and log gates f32 [C] -> T f32: algorithmic bytes 256C + 8C + 4C^2 "
                               "per chunk; A (bf16 [C,C]) never written or read"}
     del kk, bb, gg
+    if args.allgather and world > 1:
+        import torch.distributed as dist
+        # every rank ends with all ranks' T ([world * chunks, C, C]); the only collective of the path
+        gathered = torch.empty((world,) + tuple(T.shape), dtype=T.dtype, device=dev)
+        ag = lambda: dist.all_gather_into_tensor(gathered, T)
+        t_ag = max_over_ranks(statistics.mean(timed_steps(ag, max(3, steps // 2), 2, flush, world, stream)), world)
+        res["allgather"] = {"ms": t_ag * 1e3, "bytes": world * T.numel() * T.element_size(),
+                            "chunks_per_s_incl_allgather": n_chunks * world / (t + t_ag)}
+        del gathered
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_gdn_baseline(A)
     if not secondary:
@@ -611,9 +620,11 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "gdn", "decode", "per_group"], default="gemm")
-    ap.add_argument("--m", type=int, default=4096)
-    ap.add_argument("--k", type=int, default=4096)
-    ap.add_argument("--n", type=int, default=14336)
+    # --gemm-m / --gemm-n: the same options under names that torchrun's own parser does not take for
+    # abbreviations of its --master-*/--nnodes/--nproc-per-node (a bare --m or --n under torchrun errors)
+    ap.add_argument("--m", "--gemm-m", dest="m", type=int, default=4096)
+    ap.add_argument("--k", "--gemm-k", dest="k", type=int, default=4096)
+    ap.add_argument("--n", "--gemm-n", dest="n", type=int, default=14336)
     ap.add_argument("--gdn-chunks", type=int, default=4096)
     ap.add_argument("--allgather", action="store_true")
     ap.add_argument("--no-gdn", action="store_true")
