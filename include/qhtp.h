@@ -159,10 +159,17 @@ QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan *plan, const void *act, uint32_t
  * and returns QHTP_STATUS_INVALID_ARGUMENT with a qhtp_last_error_string message otherwise.  The
  * first call on each device looks up the area's device address: make it before any stream capture.
  * All calls share the area: calls whose work overlaps on the GPU race, so serialize them.  Calls no
- * cudaMalloc / cudaFree.  Device-side pipeline timeouts are not reported by this entry point. */
+ * cudaMalloc / cudaFree.  M above 2^24 is QHTP_STATUS_UNSUPPORTED, as for qhtp_matmul_run.
+ * Device-side pipeline timeouts are recorded in the area's error word; qhtp_matmul_noalloc_check
+ * reads it. */
 #define QHTP_NOALLOC_SCRATCH_BYTES (8u << 20)
 QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
                                    void *stream);
+
+/* qhtp_matmul_check for qhtp_matmul_run_noalloc: synchronize `stream` and read (and clear) the error
+ * word an M-row qhtp_matmul_run_noalloc call on the current device wrote.  No counterpart in the
+ * reference.  Allocates nothing. */
+QhtpStatus qhtp_matmul_noalloc_check(const QhtpMatmulPlan *plan, uint32_t m, int *device_code, void *stream);
 
 /* qhtp_matmul_run from and to HOST memory: out_host[M,N] from act_host[M,K].  No counterpart in
  * the reference (its op runs on buffers the QNN runtime has placed); for serving from host memory.
@@ -184,6 +191,23 @@ QhtpStatus qhtp_matmul_run_host(const QhtpMatmulPlan *plan, const void *act_host
  * QHTP_STATUS_RUNTIME_ERROR if a kernel recorded an error (code in *device_code if non-NULL). */
 QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan *plan, void *workspace, uint32_t m, int *device_code,
                              void *stream);
+
+/* Failure-path self-test (no counterpart in the reference, whose kernels report nothing).  Launches
+ * one 4-warp CTA that waits, with the library's bounded pipeline wait, on an mbarrier that no thread
+ * arrives on.  Each wait gives up after limit_cycles (1 .. 2^32) cycles of the SM clock, records
+ * code 4 (the code of a timed-out pipeline wait) in the device word *err_word unless it is already
+ * non-zero, adds 1 per warp to the device counter *warps_gave_up, and the kernel returns.  Point
+ * err_word at a workspace's error word and qhtp_matmul_check reports QHTP_STATUS_RUNTIME_ERROR with
+ * that code, exactly as it would for a GEMM whose pipeline stalled.  Asynchronous. */
+QhtpStatus qhtp_selftest_wait_timeout(int *err_word, int *warps_gave_up, uint64_t limit_cycles, void *stream);
+
+/* Tensor-pipe rate probe (no counterpart in the reference): `ctas` CTAs (one per SM) each issue
+ * `iters` rounds of four tcgen05.mma of M = 128, N = 256 -- kind 0: kind::i8 (u8 x s8, s32
+ * accumulate, 32 bytes of K per instruction), kind 1: kind::f16 with bf16 operands (f32 accumulate,
+ * 16 elements of K) -- on shared-memory operands, with no memory traffic.  Time the launch on
+ * `stream` with CUDA events: executed ops = ctas * iters * 4 * 2 * 128 * 256 * (32 | 16).  A timed-out
+ * completion wait records code 3 in the device word *err_word.  Asynchronous. */
+QhtpStatus qhtp_selftest_mma_rate(uint32_t kind, uint32_t iters, uint32_t ctas, int *err_word, void *stream);
 
 /* Read back the prepared per-channel records (the B200 "sidecar", 32 bytes per channel, padded to
  * the tile) into host memory: sizes in bytes.  Synchronizes `stream`. */

@@ -50,14 +50,19 @@ static void solve_one(const int16_t *A, int C, double sA, double sT, double *T, 
   for (int i = 0; i < nb; ++i) {
     for (int j = i - 1; j >= 0; --j) {
       memset(acc, 0, sizeof(double) * BLK * BLK);
+      /* per (k, r, c): the BLK-term dot product is summed on its own, then added to acc -- the
+       * reference's floating-point order (gdn_solve_ref.c:46-53), so the two agree bit for bit */
       for (int k = j; k < i; ++k) {
         const double *tkj = Tb + ((size_t)k * nb + j) * BLK * BLK;
-        for (int r = 0; r < BLK; ++r)
-          for (int m = 0; m < BLK; ++m) {
-            const double a = (double)A[(size_t)(i * BLK + r) * C + k * BLK + m] * sA;
-            if (a == 0.0) continue;
-            for (int c = 0; c < BLK; ++c) acc[r * BLK + c] += a * tkj[m * BLK + c];
+        for (int r = 0; r < BLK; ++r) {
+          double a[BLK];
+          for (int m = 0; m < BLK; ++m) a[m] = (double)A[(size_t)(i * BLK + r) * C + k * BLK + m] * sA;
+          for (int c = 0; c < BLK; ++c) {
+            double s = 0.0;
+            for (int m = 0; m < BLK; ++m) s += a[m] * tkj[m * BLK + c];
+            acc[r * BLK + c] += s;
           }
+        }
       }
       const double *tii = Tb + ((size_t)i * nb + i) * BLK * BLK;
       double *tij = Tb + ((size_t)i * nb + j) * BLK * BLK;

@@ -324,14 +324,30 @@ class QuantCase:
     lpbq_expanded: np.ndarray | None = None   # [N, K] int16
     bias_float: np.ndarray | None = None      # per_group only (bias kept float there)
     ref_output_q: np.ndarray | None = None    # reference float64-formula output
+    act_zp_free: int | None = None            # a free (min/max-derived) activation zero point, else the family's
+    out_zp_free: int | None = None            # a free output zero point, else the family's
+
+    @property
+    def act_zp(self) -> int:
+        return self.family.act_zp if self.act_zp_free is None else int(self.act_zp_free)
+
+    @property
+    def out_zp(self) -> int:
+        return self.family.out_zp if self.out_zp_free is None else int(self.out_zp_free)
 
     @property
     def act_offset(self) -> int:
-        return -self.family.act_zp
+        return -self.act_zp
 
     @property
     def out_offset(self) -> int:
-        return -self.family.out_zp
+        return -self.out_zp
+
+    def with_act(self, act_q: np.ndarray) -> "QuantCase":
+        """The same weights, scales and encodings with another activation (rows, chain steps)."""
+        return QuantCase(self.family, act_q, self.weight_q, self.weight_scale, self.bias_q, self.act_scale,
+                         self.out_scale, self.lpbq_factor, self.lpbq_expanded, self.bias_float, None,
+                         self.act_zp_free, self.out_zp_free)
 
     @property
     def mma_weight(self) -> np.ndarray:
@@ -405,6 +421,52 @@ def make_baseline_case(family: str, m: int, k: int, n: int, seed: int = 0x6D6D,
     return quantize_case(fam, x, w, b, with_reference_output, fast=True, range_rows=256 if big else None)
 
 
+def qnn_asymmetric_encoding(vmin: float, vmax: float, bits: int = 8) -> tuple[float, int]:
+    """QNN/AIMET asymmetric encoding from a float range: the range is widened to hold 0,
+    scale = (max - min) / (2^bits - 1), zero point = -round(min / scale) (QNN offset = -zero point,
+    dequant (q + offset) * scale, the convention of generate_qnn_matmul_python_cases.py:203-218).
+    The zero point is then free in [0, 2^bits - 1] instead of the families' fixed 2^(bits-1)."""
+    lo, hi = min(float(vmin), 0.0), max(float(vmax), 0.0)
+    qmax = (1 << bits) - 1
+    scale = max((hi - lo) / qmax, 1.0e-12)
+    zp = int(np.clip(-np.rint(lo / scale), 0, qmax))
+    return scale, zp
+
+
+def make_free_offset_u8i8_case(m: int = 256, k: int = 256, n: int = 256, seed: int = 0x5EED0,
+                               x_shift: float = 0.0) -> QuantCase:
+    """u8i8 with free asymmetric activation and output encodings.
+
+    X ~ N(0,1) (+ x_shift, which moves the activation zero point), quantized u8 with scale
+    (max - min)/255 and zero point -round(min/scale); W ~ N(0, 0.05) quantized symmetric int8 with ONE
+    per-tensor scale max|W|/127 (given to the op as N equal per-channel scales); bias ~ N(0, 0.1)
+    quantized int32 at s_x * s_w; output Y = X W^T + b requantized u8 with the scale and zero point of
+    Y's float min/max, round half to even.  The float64 answer follows the reference oracle's
+    quantized path (generate_qnn_matmul_python_cases.py:426-481) with these encodings:
+    y = ((x_q - zp_x) s_x) @ float32(q s_w)^T + bias_q s_x s_w, out = clip(rint(y / s_o + zp_o)).
+    """
+    fam = FAMILIES["u8i8"]
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((m, k), dtype=np.float32) + np.float32(x_shift)).astype(np.float32)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    y_float = x.astype(np.float64) @ w.astype(np.float64).T + b.astype(np.float64)
+    s_x, zp_x = qnn_asymmetric_encoding(float(x.min()), float(x.max()))
+    s_o, zp_o = qnn_asymmetric_encoding(float(y_float.min()), float(y_float.max()))
+    act_q = quantize_affine(x, s_x, -zp_x, 255, np.uint8)
+    s_w = np.float32(symmetric_scale(float(w.min()), float(w.max()), 127))
+    q = np.clip(np.rint(w.astype(np.float64) / np.float64(s_w)), -127, 127).astype(np.int8)
+    scales = np.full(n, s_w, np.float32)
+    bscale = s_x * np.float64(s_w)
+    bias_q = np.clip(np.rint(b.astype(np.float64) / bscale), -(1 << 31), (1 << 31) - 1).astype(np.int32)
+    x_deq = (act_q.astype(np.float64) - zp_x) * s_x
+    w_deq = (q.astype(np.float32) * scales[:, None]).astype(np.float64)
+    y = x_deq @ w_deq.T + bias_q.astype(np.float64) * bscale
+    ref = quantize_affine(y, s_o, -zp_o, 255, np.uint8)
+    return QuantCase(fam, act_q, q, scales, bias_q, s_x, s_o, ref_output_q=ref, act_zp_free=zp_x,
+                     out_zp_free=zp_o)
+
+
 # ----------------------------------------------------------------------------------------------
 # 3. Prepared record ("sidecar") and the exact requant model
 # ----------------------------------------------------------------------------------------------
@@ -468,7 +530,7 @@ def prepare_record(case: QuantCase, dequant: str = "f32", return_c: bool = False
     if fam.schema == "per_group":
         raise NotImplementedError("per_group schema has no per-channel record")
     wq = case.mma_weight.astype(np.int64)
-    zp = fam.act_zp
+    zp = case.act_zp
     m_s, e_s = split_f32(case.weight_scale)
     rec = np.zeros(wq.shape[0], RECORD_DTYPE)
     sum_q = wq.sum(axis=1)
@@ -528,7 +590,7 @@ def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
     tpre = rec["m_q"].astype(np.int64)[None, :] * p + rec["beff"][None, :]
     if ep is not None:
         tpre += (xq @ ep.astype(np.float64).T).astype(np.int64)
-    z = tpre.astype(np.float64) * c[None, :] + fam.out_zp
+    z = tpre.astype(np.float64) * c[None, :] + case.out_zp
     r = np.rint(z)
     frac = z - np.floor(z)
     near = (np.abs(frac - 0.5) <= TIE_EPS) & (z > -1.0) & (z < fam.out_qmax + 1.0)
@@ -536,7 +598,7 @@ def exact_output(case: QuantCase, dequant: str = "f32", return_t: bool = False):
         m_s, e_s = split_f32(case.weight_scale)
         for i, j in zip(*np.nonzero(near)):
             r[i, j] = _exact_round(int(tpre[i, j]), int(mul[j]), int(e_s[j]),
-                                   case.act_scale, case.out_scale, fam.out_zp)
+                                   case.act_scale, case.out_scale, case.out_zp)
     out = np.clip(r, 0, fam.out_qmax).astype(fam.out_dtype)
     if return_t:
         return out, tpre, int(near.sum())
@@ -567,7 +629,7 @@ def per_group_output(case: QuantCase) -> np.ndarray:
     m_s, e_s = split_f32(case.weight_scale)                   # [N, G]
     p = (q.reshape(n, g_count, 64) * m_s[:, :, None]).reshape(n, k)
     ep = round_to_24_bits(p) - p                              # e' per group, |e'| <= 8
-    xz = (case.act_q.astype(np.int64) - fam.act_zp).astype(np.float64)
+    xz = (case.act_q.astype(np.int64) - case.act_zp).astype(np.float64)
     acc = np.zeros((case.act_q.shape[0], n))
     for g in range(g_count):
         sl = slice(64 * g, 64 * (g + 1))
@@ -576,13 +638,13 @@ def per_group_output(case: QuantCase) -> np.ndarray:
         z = m_s[None, :, g] * sq + se
         acc = acc + np.ldexp(z.astype(np.float64), e_s[None, :, g])
     y = case.act_scale * acc + case.bias_float.astype(np.float64)[None, :]
-    r = np.rint(y / case.out_scale + fam.out_zp)
+    r = np.rint(y / case.out_scale + case.out_zp)
     return np.clip(r, 0, fam.out_qmax).astype(fam.out_dtype)
 
 
 def integer_accumulator(case: QuantCase) -> np.ndarray:
     """sum_k (x_q - zp) * q as int64 -- the W16A16 identity target."""
-    xc = case.act_q.astype(np.int64) - case.family.act_zp
+    xc = case.act_q.astype(np.int64) - case.act_zp
     return (xc.astype(np.float64) @ case.mma_weight.astype(np.float64).T).astype(np.int64)
 
 

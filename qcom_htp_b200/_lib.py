@@ -76,6 +76,8 @@ SIGNATURES = {
                                   C.c_size_t, C.c_void_p]),
     "qhtp_matmul_run_noalloc": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p,
                                           C.c_void_p]),
+    "qhtp_matmul_noalloc_check": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_uint32, C.POINTER(C.c_int),
+                                            C.c_void_p]),
     "qhtp_matmul_run_host": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_uint32),
                                        C.c_void_p]),
@@ -84,6 +86,8 @@ SIGNATURES = {
                                          C.c_void_p, C.c_size_t, C.c_void_p]),
     "qhtp_matmul_check": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.POINTER(C.c_int),
                                     C.c_void_p]),
+    "qhtp_selftest_wait_timeout": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]),
+    "qhtp_selftest_mma_rate": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]),
     "qhtp_matmul_read_records": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_size_t, C.c_void_p]),
     "qhtp_lpbq_expand_i8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p,
                                       C.c_void_p]),

@@ -16,7 +16,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libqhtp.so"
-SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "gdn256x2.cu", "noalloc.cu", "wire.cu", "gdn256f.cu", "qgroup.cu"]
+SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "gdn256x2.cu", "noalloc.cu", "wire.cu", "gdn256f.cu", "qgroup.cu", "peak.cu"]
 HEADERS = ["ptx.cuh", "requant.cuh", "internal.h", "gdn_common.cuh"]
 
 NVCC_FLAGS = [
@@ -24,8 +24,8 @@ NVCC_FLAGS = [
     "-O3", "-lineinfo", "-std=c++17",
     "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-O2",
-    "-shared",
 ]
+OBJ_DIR = PKG.parent / "_build"
 
 
 def nvcc() -> str:
@@ -44,16 +44,33 @@ def _stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
+    """Compile every source to an object (in parallel, one nvcc per file), then link the shared
+    library.  Whole-library rebuild: the sources share headers, so nothing is reused."""
     if not force and not _stale():
         return LIB
-    cmd = [nvcc(), *NVCC_FLAGS, *(extra or []), "-o", str(LIB)] + [str(CSRC / s) for s in SOURCES]
-    if verbose:
-        print(" ".join(cmd))
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    from concurrent.futures import ThreadPoolExecutor
+    OBJ_DIR.mkdir(exist_ok=True)
+    nv = nvcc()
+
+    def compile_one(src: str):
+        obj = OBJ_DIR / (Path(src).stem + ".o")
+        cmd = [nv, *NVCC_FLAGS, *(extra or []), "-c", "-o", str(obj), str(CSRC / src)]
+        return cmd, obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 4)) as ex:
+        results = list(ex.map(compile_one, SOURCES))
+    for cmd, _, r in results:
+        if verbose:
+            print(" ".join(cmd))
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({r.returncode}):\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        if verbose and r.stderr:
+            print(r.stderr)
+    link = [nv, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(LIB),
+            *[str(o) for _, o, _ in results]]
+    r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
-    if verbose and r.stderr:
-        print(r.stderr)
+        raise RuntimeError(f"nvcc link failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

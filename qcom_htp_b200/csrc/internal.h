@@ -73,6 +73,7 @@ cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* 
 cudaError_t launch_prepare_group(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
                                  int* bad_scale, cudaStream_t stream, int sms);
 cudaError_t launch_gemm_group(const GemmLaunch& g, const uint8_t* a_base, uint64_t a_rows, int sms);
+cudaError_t launch_wait_timeout(int* err, long long limit, int* gave_up, cudaStream_t stream);
 cudaError_t launch_lpbq_expand(const uint8_t* w4, const uint8_t* bs, uint32_t k, uint32_t n, uint32_t block,
                                int8_t* out, cudaStream_t stream);
 

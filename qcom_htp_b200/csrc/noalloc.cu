@@ -64,11 +64,13 @@ extern "C" QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan* plan, const 
   if (act == nullptr || out == nullptr || m == 0) return QHTP_STATUS_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(act) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return QHTP_STATUS_INVALID_ARGUMENT;
+  if (m > (1u << 24)) return QHTP_STATUS_UNSUPPORTED;  // the row limit of qhtp_matmul_run
   const size_t need = qhtp_matmul_workspace_bytes(plan, m);  // u16 byte planes + 256-byte error area
   if (need == 0 || need > kScratchBytes) {
     qhtp::set_last_message(
-        "qhtp_matmul_run_noalloc: workspace for this M exceeds the library's fixed 8 MiB scratch "
-        "(u16 activations need 2*M*K + 256 bytes); use qhtp_matmul_run with a caller workspace");
+        "qhtp_matmul_run_noalloc: qhtp_matmul_workspace_bytes(plan, M) exceeds the library's fixed 8 MiB "
+        "scratch (u16 activations need align_up(2*M*K, 256) + 256 bytes); use qhtp_matmul_run with a "
+        "caller workspace");
     return QHTP_STATUS_INVALID_ARGUMENT;
   }
   uint8_t* scratch = nullptr;
@@ -87,4 +89,24 @@ extern "C" QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan* plan, const 
   g.err = err;
   g.stream = s;
   return qhtp::status_from_cuda(qhtp::launch_gemm(g));
+}
+
+extern "C" QhtpStatus qhtp_matmul_noalloc_check(const QhtpMatmulPlan* plan, uint32_t m, int* device_code,
+                                               void* stream) {
+  if (plan == nullptr || plan->magic != qhtp::kPlanMagic || m == 0 || m > (1u << 24))
+    return QHTP_STATUS_INVALID_ARGUMENT;
+  const size_t need = qhtp_matmul_workspace_bytes(plan, m);
+  if (need == 0 || need > kScratchBytes) return QHTP_STATUS_INVALID_ARGUMENT;
+  uint8_t* scratch = nullptr;
+  cudaError_t e = scratch_on_current_device(&scratch);
+  if (e != cudaSuccess) return qhtp::status_from_cuda(e);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* err = reinterpret_cast<int*>(scratch + need - 256);  // where an M-row call keeps its error word
+  int h = 0;
+  e = cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return qhtp::status_from_cuda(e);
+  if (device_code) *device_code = h;
+  return h == 0 ? QHTP_STATUS_OK : QHTP_STATUS_RUNTIME_ERROR;
 }

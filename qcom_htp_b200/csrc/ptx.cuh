@@ -64,18 +64,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.  Returns false on timeout (and
-// records `code` in *err).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Bounded wait for the phase with the given parity to complete, giving up after `limit` cycles of
+// %clock64.  Returns false on timeout (and records `code` in *err).
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > QHTP_SPIN_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       record_error(err, code);
       return false;
     }
   }
+}
+
+// The kernels' wait: bounded at QHTP_SPIN_LIMIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, QHTP_SPIN_LIMIT_CYCLES);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -339,6 +339,14 @@ QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan* plan, void* workspace, uint32
   return h == 0 ? QHTP_STATUS_OK : QHTP_STATUS_RUNTIME_ERROR;
 }
 
+QhtpStatus qhtp_selftest_wait_timeout(int* err_word, int* warps_gave_up, uint64_t limit_cycles, void* stream) {
+  if (err_word == nullptr || warps_gave_up == nullptr || limit_cycles == 0 || limit_cycles > (1ull << 32))
+    return QHTP_STATUS_INVALID_ARGUMENT;
+  if (!aligned(err_word, 4) || !aligned(warps_gave_up, 4)) return QHTP_STATUS_INVALID_ARGUMENT;
+  return from_cuda(launch_wait_timeout(err_word, static_cast<long long>(limit_cycles), warps_gave_up,
+                                       as_stream(stream)));
+}
+
 QhtpStatus qhtp_matmul_read_records(const QhtpMatmulPlan* plan, void* host_dst, size_t bytes, void* stream) {
   if (!plan_ok(plan) || plan->prepared == nullptr || host_dst == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
   if (plan->mode == kModeGroup) return QHTP_STATUS_UNSUPPORTED;  // per-(channel, group) constants, no record

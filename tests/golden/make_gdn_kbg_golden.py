@@ -21,7 +21,9 @@ ROOT = Path(__file__).resolve().parents[2]
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit(f"usage: python {Path(__file__).name} <reference checkout>")
+    ref = Path(sys.argv[1])
     sys.dont_write_bytecode = True
     sys.path.insert(0, str(ref / "scripts"))
     sys.path.insert(0, str(ROOT))

@@ -40,7 +40,9 @@ def load_reference(ref: Path):
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit(f"usage: python {Path(__file__).name} <reference checkout>")
+    ref = Path(sys.argv[1])
     G = load_reference(ref)
     rng = np.random.default_rng(0x31E)
     w4 = rng.integers(-8, 8, size=(K, N)).astype(np.int32)        # logical int4 [K, N]

@@ -204,3 +204,57 @@ def test_gdn_A_from_kbg_matches_reference_chunk_kernel():
     A = G.chunk_A_from_kbg(z["k"], z["beta"], z["g_tok"])
     T = G.inverse_fp64(A)
     assert np.abs(T - z["T"]).max() < 1e-12
+
+
+def test_gdn_c_port_matches_reference_solver_binary(tmp_path):
+    """The timed CPU baseline (oracle/gdn_block_ref.c) against the reference's own scalar solver
+    (example/gdn_native/solve_op/gdn_solve_ref.c:17-84, compiled unmodified into oracle/_ref by
+    oracle/Makefile) on shared inputs: the same file formats the reference's main() reads
+    (dims.i32, A_codes.i16, sA.f32, sT.f32 -> T_out.f64).  Equal bit for bit."""
+    import ctypes
+    import subprocess
+    odir = Path(G.__file__).parent
+    ref_bin = odir / "_ref" / "gdn_solve_ref"
+    lib_path = odir / "libgdn_block_ref.so"
+    if not ref_bin.exists() or not lib_path.exists():
+        pytest.skip("oracle/_ref/gdn_solve_ref or oracle/libgdn_block_ref.so not built (make -C oracle [ref])")
+    for C, seed in ((64, 5), (256, 6)):
+        A = G.make_chunk_A(3, C=C, seed=seed)
+        H = A.shape[0]
+        sA = (np.abs(A).reshape(H, -1).max(axis=1) / 32767.0).astype(np.float32)   # one scale per head
+        Aq = np.clip(np.rint(A / sA[:, None, None]), -32767, 32767).astype(np.int16)
+        sT = np.float32(2.0 / 32767.0)
+        np.array([H, C], np.int32).tofile(tmp_path / "dims.i32")
+        Aq.tofile(tmp_path / "A_codes.i16")
+        sA.tofile(tmp_path / "sA.f32")
+        np.array([sT], np.float32).tofile(tmp_path / "sT.f32")
+        subprocess.run([str(ref_bin)], cwd=tmp_path, check=True, capture_output=True)
+        want = np.fromfile(tmp_path / "T_out.f64", np.float64).reshape(H, C, C)
+        lib = ctypes.CDLL(str(lib_path))
+        got = np.zeros((H, C, C), np.float64)
+        rc = lib.gdn_block_ref_solve(Aq.ctypes.data_as(ctypes.c_void_p), sA.ctypes.data_as(ctypes.c_void_p),
+                                     ctypes.c_float(sT), H, C, got.ctypes.data_as(ctypes.c_void_p), 2)
+        assert rc == 0
+        np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("shift", [0.0, 1.5, -2.0, 3.0])
+def test_free_offset_u8i8_exact_model_matches_float64_path(shift):
+    """BASELINE configs[0] (u8i8, QNN free-offset asymmetric activation/output encodings, per-tensor
+    int8 weights): the exact integer model equals the reference oracle's float64 quantized path on
+    every element, at activation zero points far from the families' fixed 128."""
+    c = O.make_free_offset_u8i8_case(256, 256, 256, seed=11, x_shift=shift)
+    assert 0 <= c.act_zp <= 255 and 0 <= c.out_zp <= 255
+    assert len(set(c.weight_scale.tolist())) == 1                   # one per-tensor scale
+    np.testing.assert_array_equal(O.exact_output(c), c.ref_output_q)
+    if shift != 0.0:
+        assert c.act_zp != 128
+
+
+def test_qnn_asymmetric_encoding_rules():
+    s, zp = O.qnn_asymmetric_encoding(-1.0, 3.0)
+    assert s == 4.0 / 255 and zp == 64                  # -round(-1 / (4/255)) = round(63.75) = 64
+    s, zp = O.qnn_asymmetric_encoding(0.5, 2.0)         # range widened to hold 0: zero point 0
+    assert s == 2.0 / 255 and zp == 0
+    s, zp = O.qnn_asymmetric_encoding(-2.0, -0.5)
+    assert zp == 255

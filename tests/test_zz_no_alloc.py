@@ -56,3 +56,53 @@ def test_noalloc_rejects_oversized_workspace():
                                        torch.cuda.current_stream().cuda_stream)
     assert st == L.INVALID_ARGUMENT
     assert b"8 MiB" in L.lib.qhtp_last_error_string()
+
+
+def _status(op, act_ptr, m, out_ptr, plan=True):
+    from qcom_htp_b200 import _lib as L
+    return L.lib.qhtp_matmul_run_noalloc(C.byref(op.plan) if plan else None, act_ptr, m, out_ptr,
+                                         torch.cuda.current_stream().cuda_stream)
+
+
+def test_noalloc_host_argument_checks():
+    """The host-side checks that stand in for the caller workspace's: null plan, zero rows,
+    16-byte-misaligned activation or output, and the 2^24-row limit of qhtp_matmul_run (for u8
+    activations the scratch size alone would not bound M).  All rejected before any launch."""
+    from qcom_htp_b200 import _lib as L
+    c = O.generate_case("u8i8", "normal_random", 64, 128, 64)
+    op = build_op(c)
+    act = torch.zeros((65, 128), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((65, 64), dtype=torch.uint8, device="cuda")
+    a, o = act.data_ptr(), out.data_ptr()
+    assert _status(op, a, 64, o, plan=False) == L.INVALID_ARGUMENT
+    assert _status(op, a, 0, o) == L.INVALID_ARGUMENT
+    assert _status(op, a + 8, 64, o) == L.INVALID_ARGUMENT
+    assert _status(op, a, 64, o + 8) == L.INVALID_ARGUMENT
+    assert _status(op, a, (1 << 24) + 1, o) == L.UNSUPPORTED       # rejected on the host: no big buffers
+    torch.cuda.synchronize()
+    code = C.c_int(-1)
+    assert L.lib.qhtp_matmul_noalloc_check(C.byref(op.plan), 0, C.byref(code), None) == L.INVALID_ARGUMENT
+
+
+def test_noalloc_u8_rows_beyond_u16_limit_and_error_word():
+    """u8 activations need no byte planes, so M may exceed what a u16 activation could use (here
+    M = 8192, K = 1024: a u16 activation would need 16 MiB of planes).  Output equals
+    qhtp_matmul_run's byte for byte on two calls in a row, and the error word the no-alloc calls keep
+    in the library's scratch reads back as clear."""
+    from qcom_htp_b200 import _lib as L
+    m, k, n = 8192, 1024, 256
+    c = O.make_baseline_case("u8i8", m, k, n, seed=0x8A)
+    op = build_op(c)
+    act = to_dev(c.act_q)
+    for _ in range(2):
+        want = op(act)
+        got = _noalloc(op, act)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    code = C.c_int(-1)
+    st = L.lib.qhtp_matmul_noalloc_check(C.byref(op.plan), m, C.byref(code),
+                                         torch.cuda.current_stream().cuda_stream)
+    assert st == L.OK and code.value == 0
+    rows = np.r_[0:32, 8160:8192]
+    sub = O.QuantCase(c.family, c.act_q[rows], c.weight_q, c.weight_scale, c.bias_q, c.act_scale, c.out_scale)
+    np.testing.assert_array_equal(got.cpu().numpy()[rows], O.exact_output(sub))
