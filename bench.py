@@ -567,8 +567,11 @@ def cpu_gdn_baseline(A: torch.Tensor, budget_s: float = 10.0) -> dict:
 # ----------------------------------------------------------------------------------------------
 def executed_multiplier(op) -> int:
     """Tensor-pipe work per logical op: activation byte planes x weight planes ([q | e'] in the
-    float32-dequant mode, [hi | lo] for int16 weights; one plane in the exact mode)."""
+    float32-dequant mode, [hi | lo] for int16 weights; one plane in the exact mode).  With the
+    lo-plane residual bound (plan flag 1) the lo activation plane multiplies the q rows only: 3."""
     planes_w = 2 if int(op.plan.mode) in (0, 2) else 1
+    if int(op.plan.mode) == 0 and int(op.plan.a_planes) == 2 and int(op.plan.flags) & 1:
+        return 3
     return int(op.plan.a_planes) * planes_w
 
 
@@ -693,7 +696,8 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     e2e_ok = torch.equal(out_h, out.cpu())
     rf = row["roofline"]
     rf["traffic"] = NCU_TRAFFIC_BYTES.get(("qgemm", m, k, d["n"]))
-    rf["kernel"] = "split_u16_planes + qgemm_kernel<2,F32> (one qhtp_matmul_run)"
+    rf["kernel"] = ("split_u16_planes + qgemm_kernel<2,F32" + (",LO3" if int(op.plan.flags) & 1 else "") +
+                  "> (one qhtp_matmul_run)")
     res = {
         "metric": "w4a16_lpbq_gemm_tops", "value": ops_total / t_step / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": row["ms_per_step"], "higher_is_better": True,

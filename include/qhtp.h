@@ -116,6 +116,7 @@ typedef struct QhtpMatmulPlan {
   double act_scale, out_scale;
   uint64_t act_mant;      /* act_scale = act_mant * 2^act_exp2, 53-bit mantissa */
   int32_t act_exp2;
+  uint32_t flags;         /* kernel options chosen by qhtp_matmul_prepare from the prepared weights */
   uint64_t out_mant;
   int32_t out_exp2;
   uint64_t plane_bytes;   /* prepared weight planes */

@@ -472,7 +472,7 @@ def make_free_offset_u8i8_case(m: int = 256, k: int = 256, n: int = 256, seed: i
 # ----------------------------------------------------------------------------------------------
 
 RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cmn", "<u8"), ("m_q", "<i4"), ("wbits", "<u4"),
-                         ("tn", "<i4"), ("pad", "<i4")])   # 32 bytes / output channel
+                         ("tn", "<i4"), ("lo_win", "<i4")])   # 32 bytes / output channel
 
 
 def split_f32(scale: np.ndarray):
@@ -525,6 +525,11 @@ def prepare_record(case: QuantCase, dequant: str = "f32", return_c: bool = False
     m_q   : multiplier of the q-plane accumulator inside T (m_s in f32 mode, 1 in exact mode)
     wbits : the float32 weight scale's bits (its mantissa m_s and exponent e_s feed the exact tie
             check: z* - zp_out = T*mul*mant(s_A)*2**(e_s + exp(s_A)) / s_O, mul = 1 or m_s)
+    lo_win: f32 mode with u16 activations: a bound on the lo-byte-plane x e' part of T, in output
+            units of 2**-30: |sum_k x_lo*e'| * c <= 255 * sum_k |e'| * c, stored as
+            ceil(255 * sum|e'| * c * 2**30) + 1 (capped at 2**30), the products rounded in that order;
+            0 otherwise.  A GEMM may leave that product out of its MMAs and compute it exactly only
+            for the elements whose value lies within this window of a rounding boundary.
     """
     fam = case.family
     if fam.schema == "per_group":
@@ -542,6 +547,10 @@ def prepare_record(case: QuantCase, dequant: str = "f32", return_c: bool = False
         c = np.ldexp(np.float64(case.act_scale), e_s) / np.float64(case.out_scale)
         rec["m_q"] = m_s
         mul = np.ones_like(m_s)
+        if fam.act_bits == 16:
+            sum_abs = np.abs(ep.astype(np.int64)).sum(axis=1)
+            x = (255 * sum_abs).astype(np.float64) * c * 1073741824.0
+            rec["lo_win"] = np.where(x >= 1073741824.0, 1 << 30, np.ceil(np.minimum(x, 2.0 ** 30)).astype(np.int64) + 1)
     elif dequant == "exact":
         ep = None
         rec["beff"] = bias - zp * sum_q

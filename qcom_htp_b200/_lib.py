@@ -39,7 +39,7 @@ class QhtpMatmulPlan(C.Structure):
         ("n_tiles", C.c_uint32), ("k_pad", C.c_uint32),
         ("act_zp", C.c_int32), ("out_zp", C.c_int32), ("out_qmax", C.c_int32),
         ("act_scale", C.c_double), ("out_scale", C.c_double),
-        ("act_mant", C.c_uint64), ("act_exp2", C.c_int32),
+        ("act_mant", C.c_uint64), ("act_exp2", C.c_int32), ("flags", C.c_uint32),
         ("out_mant", C.c_uint64), ("out_exp2", C.c_int32),
         ("plane_bytes", C.c_uint64), ("record_bytes", C.c_uint64), ("prepared_bytes", C.c_uint64),
         ("prepared", C.c_void_p),

@@ -19,6 +19,13 @@ enum GemmMode : uint32_t {
                    // weight image = [q (128 ch) | e' (128 ch)], s8; qgroup.cu
 };
 
+// QhtpMatmulPlan.flags (set by qhtp_matmul_prepare)
+constexpr uint32_t kPlanLoResidualByBound = 1u;  // the lo-plane x e' product is left out of the MMAs and
+                                                 // bounded per channel (ChannelRecord::lo_win); elements
+                                                 // within that bound of a rounding boundary get it exactly
+constexpr int32_t kLoWinMax = 1 << 20;           // widest per-channel window that enables it (~1e-3 units)
+constexpr int kSumsPerChannel = 4;               // prepare scratch: sum q, sum e', sum |e'|, unused
+
 constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
 constexpr int kTileN = 128;      // output channels per tile
 constexpr int kTileK = 128;      // bytes of K per pipeline stage (one 128-byte swizzle row)
@@ -41,7 +48,8 @@ struct ChannelRecord {  // 32 bytes, one per output channel (padded to the tile)
   int32_t m_q;          // multiplier of the q-plane accumulator inside T
   uint32_t wbits;       // float32 weight-scale bits: mantissa/exponent for the exact tie check
   int32_t tn;           // left shift of |T| in the fast path
-  int32_t pad;
+  int32_t lo_win;       // f32 mode, u16 activation: bound on |sum_k x_lo * e'| * c in 2^-30 output
+                        // units, ceil(255 * sum_k |e'| * c * 2^30) + 1 (capped at 2^30); else 0
 };
 static_assert(sizeof(ChannelRecord) == 32, "record layout");
 
@@ -62,6 +70,11 @@ void set_last_message(const char* msg);
 
 // qgemm.cu
 cudaError_t launch_gemm(const GemmLaunch& g);
+// u16 activation [total elements] -> byte planes hi [total] | lo [total] at `planes`
+cudaError_t launch_split_u16(const uint16_t* act, uint8_t* planes, size_t total, cudaStream_t stream);
+// qchain.cu: CHAIN=N in one kernel (K == N <= 256, act width == out width, not per-group)
+bool chain_fusable(const QhtpMatmulPlan* plan);
+cudaError_t launch_chain(const GemmLaunch& g, uint32_t chain);
 // qdecode.cu: channel-major (swap-AB) kernel for M <= kDecodeMaxM activation rows; a_base is the
 // u8 activation or the [hi; lo] byte planes of a u16 activation
 constexpr uint32_t kDecodeMaxM = 128;

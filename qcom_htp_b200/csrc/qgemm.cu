@@ -97,7 +97,9 @@ static int sm_count() {
 // GEMM kernel
 // ------------------------------------------------------------------------------------------------
 struct GemmParams {
-  int M, N, m_tiles, n_tiles, kblocks, a_plane_rows;
+  int M, N, m_tiles, n_tiles, kblocks, a_plane_rows, K;
+  const uint8_t* a_lo;      // the activation's lo byte plane [M][K] (u16 activations)
+  const int8_t* wplanes;    // the prepared weight images (the e' rows are read by the exact fix-up)
   const ChannelRecord* rec;
   void* out;
   int zp_out, qmax;
@@ -158,9 +160,35 @@ __device__ __forceinline__ bool epi_bar_and(bool v) {
   return r != 0;
 }
 
-template <int PA, int MODE>
+// sum_k x_lo[mm, k] * e'[nn, k] over the real K, by the whole warp (lane l takes the 16-byte chunks
+// l, l + 32, ...: u8 activation bytes times s8 residuals, 4 per dp4a), returned to every lane.
+__device__ __forceinline__ int32_t lo_residual_dot(const GemmParams& p, int mm, int nn, int lane) {
+  const uint8_t* xr = p.a_lo + static_cast<size_t>(mm) * p.K;
+  const int nt = nn / kTileN, rr = nn % kTileN;
+  const int8_t* wr = p.wplanes + (static_cast<size_t>(nt) * p.kblocks * 256 + 128 + rr) * kTileK;
+  int32_t acc = 0;
+  for (int ch = lane; ch < p.K / 16; ch += 32) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + ch * 16);
+    const uint4 ev = *reinterpret_cast<const uint4*>(wr + static_cast<size_t>(ch >> 3) * 256 * kTileK +
+                                                     ((((ch & 7) ^ rr) & 7) << 4));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.x), "r"(ev.x));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.y), "r"(ev.y));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.z), "r"(ev.z));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.w), "r"(ev.w));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  return acc;
+}
+
+// LO3 (u16 activation, f32 dequant, plan flag kPlanLoResidualByBound): the lo-plane MMA multiplies
+// the q rows only (N = 128); the lo x e' part of T, at most ChannelRecord::lo_win output units of
+// 2^-30, is added exactly (lo_residual_dot) only where the fast path's value lies within that
+// window of a rounding boundary.
+template <int PA, int MODE, bool LO3 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  static_assert(!LO3 || (PA == 2 && MODE == kModeF32), "LO3 is the u16-activation f32-dequant variant");
   using Cfg = GemmCfg<PA, MODE>;
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kTmemCols = 512;
@@ -274,9 +302,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             constexpr int N = Cfg::kBRows;  // 256 = [q | e'] (f32 mode), 128 = q (exact mode)
             constexpr uint32_t id = idesc_i8(128, N, 0, 1);
+            constexpr uint32_t id_lo = idesc_i8(128, LO3 ? 128 : N, 0, 1);  // LO3: lo plane x q rows only
             if (do_hi) mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
             if constexpr (PA == 2) {
-              if (do_lo) mma_i8(tmem + N, dA1 + ko, dB + ko, id, acc);
+              if (do_lo) mma_i8(tmem + N, dA1 + ko, dB + ko, id_lo, acc);
             }
           }
         }
@@ -377,7 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint32_t lq[16], le[16];
           tmem_ld16(tl + N + c0, lq);                                    // sum x_lo * q
-          if constexpr (MODE == kModeF32) tmem_ld16(tl + N + 128 + c0, le);  // sum x_lo * e'
+          if constexpr (MODE == kModeF32 && !LO3) tmem_ld16(tl + N + 128 + c0, le);  // sum x_lo * e'
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -385,7 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int64_t pq = static_cast<int64_t>(static_cast<int32_t>(hq)) * 256 + static_cast<int32_t>(lq[j]);
             if constexpr (MODE == kModeF32) {
               const uint32_t he = c0 < 32 ? se0[c0 + j] : se1[c0 - 32 + j];
-              const int64_t pe = static_cast<int64_t>(static_cast<int32_t>(he)) * 256 + static_cast<int32_t>(le[j]);
+              const int64_t pe = static_cast<int64_t>(static_cast<int32_t>(he)) * 256 +
+                                 (LO3 ? 0 : static_cast<int32_t>(le[j]));
               T[c0 + j] = static_cast<int64_t>(mqv[j]) * pq + pe;
             } else {
               T[c0 + j] = pq;
@@ -432,12 +462,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       // ---- requant + store, 16 channels per iteration; the register array rotates by 16 so the
-      // loop body is emitted once (small instruction footprint)
+      // loop body is emitted once (small instruction footprint).  The whole warp runs every
+      // iteration (rows past M compute and store nothing) so that the LO3 fix-up can be cooperative.
       const bool row_ok = m < p.M;
 #pragma unroll 1
       for (int c0 = 0; c0 < 64; c0 += 16) {
         const int n = n0 + c0;
-        if (row_ok && n < p.N) {  // channels past N (tile padding) have no record
+        if (n < p.N) {  // channels past N (tile padding) have no record; uniform across the warp
           uint32_t code[16];
           uint32_t near_mask = 0;
           int64_t fl[16];
@@ -449,9 +480,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             T[j] += static_cast<int64_t>((static_cast<uint64_t>(rb.y) << 32) | rb.x);  // + effective bias
             bool nr;
             code[j] = static_cast<uint32_t>(requant_fast96s(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
+            if constexpr (LO3) {
+              // the missing lo x e' term moves the value by at most lo_win units of 2^-30: flag the
+              // elements whose fraction lies within lo_win + 2 units of a rounding boundary
+              const uint32_t w = static_cast<uint32_t>(rec[c0 + j].lo_win) + 2u;
+              const uint32_t win = static_cast<uint32_t>(fl[j]) & 0x3FFFFFFFu;
+              const int64_t top = T[j] >> (63 - tn);
+              const bool big = (top != 0) & (top != -1);
+              nr = !big && (((win + w) & 0x3FFFFFFFu) < 2u * w);
+            }
             near_mask |= nr ? (1u << j) : 0u;
           }
-          if (near_mask != 0) {  // rare: within 2^-29 of a tie -> exact decision
+          if (!row_ok) near_mask = 0;
+          if constexpr (LO3) {
+            // exact lo x e' sums of the flagged elements, one element at a time by the whole warp,
+            // added into T (which is then complete for those elements)
+            uint32_t pending = near_mask;
+            while (true) {
+              const uint32_t lanes = __ballot_sync(0xffffffffu, pending != 0);
+              if (lanes == 0) break;
+              const int src = __ffs(lanes) - 1;
+              const int jj = __shfl_sync(0xffffffffu, __ffs(pending) - 1, src);
+              const int mm = __shfl_sync(0xffffffffu, m, src);
+              const int32_t dot = lo_residual_dot(p, mm, n + jj, lane);
+              if (lane == src) {
+                pending &= ~(1u << jj);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) T[j] += j == jj ? dot : 0;
+              }
+            }
+            if (near_mask != 0) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (near_mask & (1u << j)) {
+                  const uint64_t cmn = rec[c0 + j].cmn;
+                  const int tn = rec[c0 + j].tn;
+                  bool nr;  // T is complete: the exact decision of the full-MMA kernel
+                  code[j] = static_cast<uint32_t>(requant_fast96s(T[j], cmn, tn, p.zp_out, p.qmax, &nr, &fl[j]));
+                  if (nr) {
+                    const uint32_t wb = rec[c0 + j].wbits;
+                    const int es = static_cast<int>((wb >> 23) & 0xFFu) - 150;
+                    code[j] = static_cast<uint32_t>(requant_tie_w(T[j], fl[j], 1u, es + p.act_exp2, p.act_mant,
+                                                                p.out_mant, p.out_exp2, p.zp_out, p.qmax));
+                  }
+                }
+              }
+            }
+          } else if (near_mask != 0) {  // rare: within 2^-29 of a tie -> exact decision
             for (int j = 0; j < 16; ++j) {
               if (near_mask & (1u << j)) {
                 const uint32_t wb = rec[c0 + j].wbits;
@@ -465,7 +540,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (n + 8 * h < p.N) {
+            if (row_ok && n + 8 * h < p.N) {
               const uint32_t* cd = code + 8 * h;
               if (u16) {
                 uint4 v;
@@ -523,13 +598,13 @@ __global__ void split_u16_planes(const uint16_t* __restrict__ act, uint8_t* __re
   }
 }
 
-template <int PA, int MODE>
+template <int PA, int MODE, bool LO3 = false>
 static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, const CUtensorMap& tb,
                                   const GemmParams& prm) {
   using Cfg = GemmCfg<PA, MODE>;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<PA, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<PA, MODE, LO3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmem);
     if (e != cudaSuccess) return e;
     attr_done = true;
@@ -546,7 +621,16 @@ static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PA == 2 ? 1 : 0;  // only behind this library's own plane split
-  return cudaLaunchKernelEx(&cfg, qgemm_kernel<PA, MODE>, ta, tb, prm);
+  return cudaLaunchKernelEx(&cfg, qgemm_kernel<PA, MODE, LO3>, ta, tb, prm);
+}
+
+cudaError_t launch_split_u16(const uint16_t* act, uint8_t* planes, size_t total, cudaStream_t stream) {
+  const size_t n8 = total / 8;
+  int blocks = static_cast<int>((n8 + 255) / 256);
+  if (blocks > sm_count() * 16) blocks = sm_count() * 16;
+  if (blocks < 1) blocks = 1;
+  split_u16_planes<<<blocks, 256, 0, stream>>>(act, planes, planes + total, n8);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(const GemmLaunch& g) {
@@ -557,13 +641,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   uint64_t a_rows;
   if (pl->a_planes == 2) {
     const size_t total = static_cast<size_t>(g.m) * K;
-    const size_t n8 = total / 8;
-    int blocks = static_cast<int>((n8 + 255) / 256);
-    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
-    if (blocks < 1) blocks = 1;
-    split_u16_planes<<<blocks, 256, 0, g.stream>>>(static_cast<const uint16_t*>(g.act), g.planes,
-                                                   g.planes + total, n8);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_split_u16(static_cast<const uint16_t*>(g.act), g.planes, total, g.stream);
     if (e != cudaSuccess) return e;
     a_base = g.planes;
     a_rows = 2ull * g.m;
@@ -584,6 +662,9 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   prm.n_tiles = static_cast<int>(pl->n_tiles);
   prm.kblocks = static_cast<int>(pl->k_pad / kTileK);
   prm.a_plane_rows = static_cast<int>(g.m);
+  prm.K = static_cast<int>(K);
+  prm.a_lo = pl->a_planes == 2 ? a_base + static_cast<size_t>(g.m) * K : nullptr;
+  prm.wplanes = reinterpret_cast<const int8_t*>(planes);
   prm.rec = reinterpret_cast<const ChannelRecord*>(planes + pl->plane_bytes);
   prm.out = g.out;
   prm.zp_out = pl->out_zp;
@@ -595,7 +676,9 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   prm.err = g.err;
   switch (pl->mode * 2 + (pl->a_planes - 1)) {
     case kModeF32 * 2 + 0: return launch_variant<1, kModeF32>(g, ta, tb, prm);
-    case kModeF32 * 2 + 1: return launch_variant<2, kModeF32>(g, ta, tb, prm);
+    case kModeF32 * 2 + 1:
+      if (pl->flags & kPlanLoResidualByBound) return launch_variant<2, kModeF32, true>(g, ta, tb, prm);
+      return launch_variant<2, kModeF32>(g, ta, tb, prm);
     case kModeExact * 2 + 0: return launch_variant<1, kModeExact>(g, ta, tb, prm);
     case kModeExact * 2 + 1: return launch_variant<2, kModeExact>(g, ta, tb, prm);
     case kModeW16 * 2 + 1: return launch_variant<2, kModeW16>(g, ta, tb, prm);
@@ -611,7 +694,7 @@ struct PrepParams {
   const void* weight;
   const uint8_t* lpbq;
   int8_t* planes;
-  long long* sums;  // [Npad][2]
+  long long* sums;  // [Npad][kSumsPerChannel]
 };
 
 __device__ __forceinline__ int load_weight(const PrepParams& p, uint32_t n, uint32_t k) {
@@ -646,7 +729,7 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
     const size_t blk = (static_cast<size_t>(tile) * (p.k_pad / kTileK) + kb) * p.b_rows * kTileK;
     int8_t* r0 = p.planes + blk + rr * kTileK + (((c ^ rr) & 7u) << 4);
     int8_t* r1 = r0 + 128 * kTileK;  // second plane (f32 / W16 modes): rows 128..255 of the image
-    long long sq = 0, se = 0;
+    long long sq = 0, se = 0, sa = 0;
     if (p.mode == kModeF32) {
       const uint32_t bits = __float_as_uint(scale[n]);
       const int32_t ms = static_cast<int32_t>((bits & 0x7FFFFFu) | 0x800000u);
@@ -660,6 +743,7 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
         r1[j] = static_cast<int8_t>(e);
         sq += q;
         se += e;
+        sa += e < 0 ? -e : e;
       }
     } else if (p.mode == kModeExact) {
 #pragma unroll 4
@@ -677,22 +761,24 @@ __global__ void prepare_planes_kernel(PrepParams p, const float* __restrict__ sc
         sq += q;
       }
     }
-    atomicAdd(reinterpret_cast<unsigned long long*>(&p.sums[2 * n]), static_cast<unsigned long long>(sq));
-    atomicAdd(reinterpret_cast<unsigned long long*>(&p.sums[2 * n + 1]), static_cast<unsigned long long>(se));
+    long long* sn = p.sums + kSumsPerChannel * n;
+    atomicAdd(reinterpret_cast<unsigned long long*>(sn), static_cast<unsigned long long>(sq));
+    atomicAdd(reinterpret_cast<unsigned long long*>(sn + 1), static_cast<unsigned long long>(se));
+    if (sa != 0) atomicAdd(reinterpret_cast<unsigned long long*>(sn + 2), static_cast<unsigned long long>(sa));
   }
 }
 
 __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* __restrict__ scale,
                                        const int32_t* __restrict__ bias, const long long* __restrict__ sums,
                                        double act_scale, double out_scale, int32_t act_zp, int32_t act_exp2,
-                                       ChannelRecord* __restrict__ rec, int* bad_scale) {
+                                       uint32_t a_planes, ChannelRecord* __restrict__ rec, int* bad_scale) {
   const uint32_t n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   const float s = scale[n];
   const uint32_t bits = __float_as_uint(s);
   const uint32_t ex = (bits >> 23) & 0xFFu;
   ChannelRecord r;
-  r.pad = 0;
+  r.lo_win = 0;
   r.wbits = bits;
   if ((bits >> 31) != 0 || ex == 0 || ex == 0xFF) {  // negative, zero/subnormal, inf/nan
     atomicCAS(bad_scale, 0, 1);
@@ -705,13 +791,21 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
   }
   const int64_t ms = static_cast<int64_t>((bits & 0x7FFFFFu) | 0x800000u);
   const int es = static_cast<int>(ex) - 150;
-  const int64_t sq = sums[2 * n], se = sums[2 * n + 1];
+  const int64_t sq = sums[kSumsPerChannel * n], se = sums[kSumsPerChannel * n + 1];
+  const int64_t sa = sums[kSumsPerChannel * n + 2];
   const int64_t b = bias[n];
   double c;
   if (mode == kModeF32) {
     r.beff = ms * (b - static_cast<int64_t>(act_zp) * sq) - static_cast<int64_t>(act_zp) * se;
     c = ldexp(act_scale, es) / out_scale;
     r.m_q = static_cast<int32_t>(ms);
+    if (a_planes == 2) {
+      // |sum_k x_lo[k] e'[k]| <= 255 * sum_k |e'[k]|, in units of 2^-30 of the output scale; the
+      // products are exact or rounded once each (no contraction: no additions)
+      const double x = __dmul_rn(__dmul_rn(static_cast<double>(255 * sa), c), 1073741824.0);
+      r.lo_win = x >= 1073741824.0 ? (1 << 30) : static_cast<int32_t>(ceil(x)) + 1;
+      atomicMax(bad_scale + 1, r.lo_win);
+    }
   } else {
     r.beff = b - static_cast<int64_t>(act_zp) * sq;
     c = __dmul_rn(act_scale, static_cast<double>(s)) / out_scale;
@@ -760,7 +854,7 @@ cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* 
   ChannelRecord* rec = reinterpret_cast<ChannelRecord*>(base + plan->plane_bytes);
   prepare_records_kernel<<<static_cast<unsigned>((plan->n + 127) / 128), 128, 0, stream>>>(
       plan->mode, plan->n, w->weight_scale, w->bias_q, sums, plan->act_scale, plan->out_scale, plan->act_zp,
-      plan->act_exp2, rec, bad_scale);
+      plan->act_exp2, plan->a_planes, rec, bad_scale);
   return cudaGetLastError();
 }
 

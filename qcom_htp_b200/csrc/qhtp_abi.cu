@@ -212,7 +212,7 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   p.record_bytes = p.mode == kModeGroup ? group_rec_bytes(&p) + align_up(npad * sizeof(double), 256)
                                         : align_up(npad * sizeof(ChannelRecord), 256);
   // planes | records | per-channel sums (prepare scratch) | 256-byte status word area
-  p.prepared_bytes = p.plane_bytes + p.record_bytes + align_up(npad * 16, 256) + 256;
+  p.prepared_bytes = p.plane_bytes + p.record_bytes + align_up(npad * 8 * kSumsPerChannel, 256) + 256;
   p.prepared = nullptr;
   *plan = p;
   return QHTP_STATUS_OK;
@@ -235,11 +235,14 @@ QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan* plan, const QhtpMatmulWeights* w,
   int* dflag = reinterpret_cast<int*>(static_cast<uint8_t*>(prepared) + plan->prepared_bytes - 256);
   cudaError_t e = launch_prepare(plan, w, prepared, dflag, s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
-  int h = 0;
-  e = cudaMemcpyAsync(&h, dflag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  int h[2] = {0, 0};  // [0] bad-scale flag, [1] widest per-channel lo-plane residual window
+  e = cudaMemcpyAsync(h, dflag, sizeof(h), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
-  if (h != 0) return QHTP_STATUS_INVALID_ARGUMENT;  // a scale was zero, negative, subnormal or not finite
+  if (h[0] != 0) return QHTP_STATUS_INVALID_ARGUMENT;  // a scale was zero, negative, subnormal or not finite
+  plan->flags = 0;
+  if (plan->mode == kModeF32 && plan->a_planes == 2 && h[1] > 0 && h[1] <= kLoWinMax)
+    plan->flags |= kPlanLoResidualByBound;
   plan->prepared = prepared;
   return QHTP_STATUS_OK;
 }
@@ -393,6 +396,20 @@ QhtpStatus run_prepared(const QhtpPreparedRun* run, uint32_t family) {
   if (run->scratch.bytes < qhtp_prepared_run_scratch_bytes(pl, run->m, run->chain)) return QHTP_STATUS_INVALID_ARGUMENT;
   if (run->chain > 1 && (pl->k != pl->n || pl->act_bits != pl->out_bits)) return QHTP_STATUS_UNSUPPORTED;
   const size_t ws = qhtp_matmul_workspace_bytes(pl, run->m);
+  if (run->chain > 1 && run->m <= (1u << 24) && chain_fusable(pl)) {
+    // K == N <= 256: one kernel for the whole chain, intermediates kept in shared memory
+    if (!aligned(run->activation.data, 16) || !aligned(run->output.data, 16) || !aligned(run->scratch.data, 256))
+      return QHTP_STATUS_INVALID_ARGUMENT;
+    GemmLaunch g;
+    g.plan = pl;
+    g.act = run->activation.data;
+    g.m = run->m;
+    g.out = run->output.data;
+    g.planes = static_cast<uint8_t*>(run->scratch.data);
+    g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(run->scratch.data) + a16_plane_bytes(pl, run->m));
+    g.stream = as_stream(run->stream);
+    return from_cuda(launch_chain(g, run->chain));
+  }
   uint8_t* inter = static_cast<uint8_t*>(run->scratch.data) + ws;
   // ping-pong so that the last pass writes `output`
   const void* src = run->activation.data;

@@ -27,7 +27,7 @@ FAMILY_BITS = {"u8i8": (8, 8, 8), "w4a8": (8, 4, 8), "w8a16": (16, 8, 16), "w4a1
                "w16a16": (16, 16, 16)}
 
 RECORD_DTYPE = np.dtype([("beff", "<i8"), ("cmn", "<u8"), ("m_q", "<i4"), ("wbits", "<u4"), ("tn", "<i4"),
-                         ("pad", "<i4")])
+                         ("lo_win", "<i4")])
 
 
 def _stream_handle(stream) -> int:
