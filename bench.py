@@ -739,6 +739,9 @@ def run_gemm(args, world, rank, local, stream) -> dict:
                              "peak_gbs": peaks()["hbm_gbs"], "rows": run_decode(args, world, rank, local, stream)}
         if not args.no_per_group:
             res["per_group"] = run_per_group(args, world, rank, local, stream)
+        if not args.no_chain:
+            res["chain"] = {"workload": "CHAIN=8 at M=K=N=256 per family (gen_quant_chain.py:1612-1613)",
+                            "rows": run_chain(args, world, rank, local, stream, L2Flush(torch.device("cuda", local)))}
     return res
 
 
@@ -805,6 +808,102 @@ def run_families(args, world, rank, local, stream, flush, probe, only: str | Non
                      "roofline": row["roofline"], "cpu_baseline": row.get("cpu_baseline")})
         del op, d
         torch.cuda.empty_cache()
+    return rows
+
+
+CHAIN_ROWS = [("u8i8", "u8i8", "per_channel"), ("w4a8_per_channel", "w4a8", "per_channel"),
+              ("w4a8_lpbq", "w4a8", "lpbq"), ("w8a16", "w8a16", "per_channel"),
+              ("w4a16_per_channel", "w4a16", "per_channel"), ("w4a16_lpbq", "w4a16", "lpbq"),
+              ("w16a16", "w16a16", "per_channel")]
+
+
+def cpu_chain_baseline(d: dict, chain: int, budget_s: float = 2.0) -> dict:
+    """The reference's chain reference (gen_quant_chain.py:1542-1545): its float64 step applied
+    `chain` times, each step's requantized codes the next step's activation codes."""
+    from oracle import mm_oracle as O   # the checker; timed here as the reference CPU implementation
+    threads = blas_threads()
+    k, n = d["k"], d["n"]
+    q = d["q"].cpu().numpy()
+    scale = d["scale"].cpu().numpy()
+    if d["factor"] is not None:
+        f = d["factor"].cpu().numpy()
+        q = (q.astype(np.int16).reshape(n, k // d["block"], d["block"]) * f.astype(np.int16)[:, :, None]).reshape(n, k)
+    w_deq = (q.astype(np.float32) * scale[:, None]).astype(np.float64)
+    bias_deq = d["bias_q"].cpu().numpy().astype(np.float64) * (d["s_a"] * scale.astype(np.float64))
+    o_bits = FAMILY_BITS[d["family"]][2]
+    o_dt = np.uint16 if o_bits == 16 else np.uint8
+    act = d["act"].cpu().numpy()
+    reps, elapsed = 0, 0.0
+    t0 = time.perf_counter()
+    while elapsed < budget_s or reps == 0:
+        x = act
+        for _ in range(chain):
+            y = ((x.astype(np.float64) - d["a_zp"]) * d["s_a"]) @ w_deq.T + bias_deq
+            x = O.quantize_affine(y, d["s_o"], -d["o_zp"], (1 << o_bits) - 1, o_dt)
+        reps += 1
+        elapsed = time.perf_counter() - t0
+    return {"value": reps * chain * 2.0 * act.shape[0] * n * k / elapsed / 1e12, "unit": "TFLOP/s",
+            "cores": int(threads), "kind": "port",
+            "sample": f"{reps} chains of {chain} float64 steps at {act.shape[0]}x{k}x{n} "
+                      f"(gen_quant_chain.py:1542-1545 restated); {elapsed:.2f} s"}
+
+
+def run_chain(args, world, rank, local, stream, flush, chain: int = 8, mkn: int = 256) -> list:
+    """CHAIN=8 at M = K = N = 256 (the reference's chain gates, gen_quant_chain.py:1612-1613) per
+    family: one qhtp_<family>_run_prepared call (the fused kernel keeps the intermediate activations in
+    shared memory) against the same chain as `chain` separate GEMM calls through HBM.  Both outputs
+    are compared with each other and a row sample with the oracle's chained output."""
+    from oracle import mm_oracle as O   # the checker
+    dev = torch.device("cuda", local)
+    rows = []
+    steps = max(10, args.steps)
+    for i, (name, fam, schema) in enumerate(CHAIN_ROWS):
+        d = synth_gemm(fam, schema, mkn, mkn, mkn, seed=900 + i, device=dev, block=64 if schema == "lpbq" else 64)
+        op = make_op(d)
+        act = d["act"]
+        o_dt = torch.uint16 if FAMILY_BITS[fam][2] == 16 else torch.uint8
+        out_f = torch.empty((mkn, mkn), dtype=o_dt, device=dev)
+        scratch = torch.zeros(op.scratch_bytes(mkn, chain), dtype=torch.uint8, device=dev)
+        fused = lambda: op.run_prepared(act, out_f, chain=chain, scratch=scratch)
+        t_f = max_over_ranks(statistics.mean(timed_steps(fused, steps, args.warmup, flush, world, stream)), world)
+        bufs = [torch.empty((mkn, mkn), dtype=o_dt, device=dev) for _ in range(2)]
+
+        def unfused():
+            x = act
+            for s in range(chain):
+                op(x, bufs[s % 2])
+                x = bufs[s % 2]
+        t_u = max_over_ranks(statistics.mean(timed_steps(unfused, steps, args.warmup, flush, world, stream)), world)
+        op.check_device(mkn)
+        out_u = bufs[(chain - 1) % 2]
+        same = bool(torch.equal(out_f, out_u))
+        # the checker: the oracle's chain on a row sample (rows are independent through the chain)
+        fam_o = O.FAMILIES[ORACLE_FAMILY[(fam, schema)]]
+        if schema == "lpbq":
+            fam_o = fam_o.with_block(d["block"])
+        r = torch.from_numpy(sample_rows(mkn, 8)).to(dev)
+        q = d["q"].cpu().numpy()
+        f = d["factor"].cpu().numpy() if d["factor"] is not None else None
+        expanded = None if f is None else (q.astype(np.int16).reshape(mkn, -1, d["block"]) *
+                                           f.astype(np.int16)[:, :, None]).reshape(mkn, -1)
+        x = d["act"].index_select(0, r).cpu().numpy()
+        for _ in range(chain):
+            c = O.QuantCase(fam_o, x, q, d["scale"].cpu().numpy(), d["bias_q"].cpu().numpy(), d["s_a"], d["s_o"],
+                            f, expanded)
+            x = O.exact_output(c, dequant="exact" if fam == "w16a16" else "f32")
+        bad = int((out_f.index_select(0, r).cpu().numpy() != x).sum())
+        ops = chain * 2.0 * mkn ** 3
+        row = {"family": name, "chain": chain, "m": mkn, "k": mkn, "n": mkn,
+               "fused_us": t_f * 1e6, "unfused_us": t_u * 1e6, "speedup": t_u / t_f,
+               "tops_fused": ops / t_f / 1e12, "tops_unfused": ops / t_u / 1e12,
+               "kernel": "qchain_kernel (one launch; + split_u16_planes for u16 activations)",
+               "fused_equals_unfused": same, "bit_exact": bad == 0 and same,
+               "bit_exact_check": {"mismatches": bad, "checked": int(x.size),
+                                   "sample": f"{len(r)} rows through all {chain} steps vs the oracle's chain"}}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            row["cpu_baseline"] = cpu_chain_baseline(d, chain)
+        rows.append(row)
+        del op, d, scratch, bufs, out_f
     return rows
 
 
@@ -1031,7 +1130,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gdn", "decode", "per_group", "family", "peak"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "gdn", "decode", "per_group", "family", "peak", "chain"],
+                    default="gemm")
     ap.add_argument("--family", default="w4a8_per_channel", help="--workload family: the row name")
     # --gemm-m / --gemm-n: the same options under names that torchrun's own parser does not take for
     # abbreviations of its --master-*/--nnodes/--nproc-per-node (a bare --m or --n under torchrun errors)
@@ -1044,6 +1144,7 @@ def main() -> int:
     ap.add_argument("--no-families", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-per-group", action="store_true")
+    ap.add_argument("--no-chain", action="store_true")
     ap.add_argument("--no-probe", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -1061,6 +1162,10 @@ def main() -> int:
         res = run_gemm(args, world, rank, local, stream)
     elif args.workload == "gdn":
         res = run_gdn(args, world, rank, local, stream)
+    elif args.workload == "chain":
+        rows = run_chain(args, world, rank, local, stream, L2Flush(dev))
+        res = {"metric": "chain8_fused_tops", "n_gpus": world, "steps": max(10, args.steps), "warmup": args.warmup,
+               "higher_is_better": True, "rows": rows}
     elif args.workload == "peak":
         res = {"metric": "tcgen05_mma_rate", "n_gpus": world, **measure_mma_peak(dev)}
     elif args.workload == "family":

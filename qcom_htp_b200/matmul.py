@@ -195,6 +195,10 @@ class QuantMatMul:
         if st != L.OK:
             raise L.QhtpError(f"qhtp_matmul_check (device code {code.value})", st)
 
+    def scratch_bytes(self, m: int, chain: int = 1) -> int:
+        """Device scratch bytes run_prepared needs for M rows (qhtp_prepared_run_scratch_bytes)."""
+        return int(L.lib.qhtp_prepared_run_scratch_bytes(C.byref(self.plan), m, chain))
+
     def records(self, stream=None) -> np.ndarray:
         """The prepared per-channel records (the B200 "sidecar"), padded to the channel tile."""
         npad = int(self.plan.n_tiles) * int(self.plan.ch_per_tile)
@@ -203,11 +207,18 @@ class QuantMatMul:
             C.byref(self.plan), buf.ctypes.data, buf.nbytes, _stream_handle(stream)))
         return buf
 
-    def run_prepared(self, act: torch.Tensor, out: torch.Tensor, chain: int = 1, stream=None) -> torch.Tensor:
-        """The qhtp_<family>_run_prepared entry point (handwritten_hmx_matmul.h:46-50 counterpart)."""
+    def run_prepared(self, act: torch.Tensor, out: torch.Tensor, chain: int = 1, stream=None,
+                     scratch: torch.Tensor | None = None) -> torch.Tensor:
+        """The qhtp_<family>_run_prepared entry point (handwritten_hmx_matmul.h:46-50 counterpart).
+        chain > 1 applies the op `chain` times, each output feeding the next activation.  `scratch`:
+        a caller-owned uint8 device buffer of at least scratch_bytes(M, chain) bytes (else one is
+        allocated for the call)."""
         m = act.shape[0]
-        nbytes = int(L.lib.qhtp_prepared_run_scratch_bytes(C.byref(self.plan), m, chain))
-        scratch = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        nbytes = self.scratch_bytes(m, chain)
+        if scratch is None:
+            scratch = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        elif scratch.numel() * scratch.element_size() < nbytes or not scratch.is_contiguous():
+            raise ValueError(f"scratch must be a contiguous device buffer of at least {nbytes} bytes")
         run = L.QhtpPreparedRun(
             m=m, k=self.k, n=self.n, chain=chain,
             activation=L.QhtpConstBuffer(_ptr(act), act.numel() * act.element_size()),
