@@ -633,11 +633,14 @@ def gemm_allgather(op, d: dict, out: torch.Tensor, args, world: int, stream, flu
                    t_step: float, chunks: int = 4) -> dict:
     """The configs[4] output exchange: every rank ends with every rank's [M, N/P] slab.  (a) one NCCL
     all-gather after the GEMM; (b) the GEMM in `chunks` row chunks, chunk i's all-gather issued on a
-    second stream as soon as chunk i is done, overlapping chunk i+1's GEMM.  NCCL moves local buffers
-    only (bytes: NCCL has no 16-bit integer type)."""
+    second stream as soon as chunk i is done, overlapping chunk i+1's GEMM.  The persistent GEMM holds
+    every SM it is given, so in (b) it runs on all but `reserve` SMs (qhtp_matmul_run_ctas) and the
+    NCCL kernel of the previous chunk's gather runs on the rest; measured for a few reserves.  NCCL
+    moves local buffers only (bytes: NCCL has no 16-bit integer type)."""
     import torch.distributed as dist
     m = d["m"]
     act = d["act"]
+    sms = torch.cuda.get_device_properties(out.device).multi_processor_count
     gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=out.device)
     ag = lambda: dist.all_gather_into_tensor(gathered.view(torch.uint8), out.view(torch.uint8))
     t_ag = max_over_ranks(statistics.mean(timed_steps(ag, max(3, args.steps // 2), 2, flush, world, stream)),
@@ -648,10 +651,10 @@ def gemm_allgather(op, d: dict, out: torch.Tensor, args, world: int, stream, flu
     comm = torch.cuda.Stream(device=out.device)
     evs = [torch.cuda.Event() for _ in bounds]
 
-    def overlapped():
+    def overlapped(reserve: int):
         works = []
         for (r0, r1), part, ev in zip(bounds, parts, evs):
-            op(act[r0:r1], out[r0:r1])
+            op(act[r0:r1], out[r0:r1], max_ctas=sms - reserve)
             ev.record(stream)
             with torch.cuda.stream(comm):
                 comm.wait_event(ev)
@@ -660,16 +663,22 @@ def gemm_allgather(op, d: dict, out: torch.Tensor, args, world: int, stream, flu
         for w in works:
             w.wait()          # the launching stream waits for every gather
 
-    t_ov = max_over_ranks(statistics.mean(timed_steps(overlapped, max(3, args.steps // 2), 2, flush, world,
-                                                      stream)), world)
+    sweep = {}
+    for reserve in (8, 16, 32):
+        t = max_over_ranks(statistics.mean(timed_steps(lambda: overlapped(reserve), max(3, args.steps // 2), 2,
+                                                       flush, world, stream)), world)
+        sweep[reserve] = t
+    best = min(sweep, key=sweep.get)
+    t_ov = sweep[best]
     op.check_device(rows)
     ok = all(torch.equal(parts[i][dist.get_rank()], out[r0:r1]) for i, (r0, r1) in enumerate(bounds))
     return {"bytes_received_per_rank": (world - 1) * out.numel() * out.element_size(),
             "serial": {"allgather_ms": t_ag * 1e3, "total_ms": (t_step + t_ag) * 1e3,
                        "tops_incl_allgather": ops_total / (t_step + t_ag) / 1e12},
-            "overlapped": {"row_chunks": chunks, "total_ms": t_ov * 1e3,
+            "overlapped": {"row_chunks": chunks, "reserved_sms": best, "total_ms": t_ov * 1e3,
                            "tops_incl_allgather": ops_total / t_ov / 1e12,
-                           "vs_max_compute_gather": t_ov / max(t_step, t_ag), "own_slab_roundtrip_ok": ok}}
+                           "vs_max_compute_gather": t_ov / max(t_step, t_ag), "own_slab_roundtrip_ok": ok,
+                           "ms_by_reserved_sms": {str(k): v * 1e3 for k, v in sweep.items()}}}
 
 
 def run_gemm(args, world, rank, local, stream) -> dict:

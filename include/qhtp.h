@@ -149,6 +149,14 @@ size_t qhtp_matmul_workspace_bytes(const QhtpMatmulPlan *plan, uint32_t m);
 QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* qhtp_matmul_run with the row-tiled GEMM's persistent grid limited to max_ctas CTAs, one per SM
+ * (0: every SM), so that the other SMs stay free for work running at the same time on other streams --
+ * e.g. the NCCL all-gather of the previous row chunk's output in a sharded multi-GPU GEMM, which cannot
+ * start while the GEMM holds every SM.  The output is the same bytes as qhtp_matmul_run's.  No
+ * counterpart in the reference (its HTP ops run alone on the device). */
+QhtpStatus qhtp_matmul_run_ctas(const QhtpMatmulPlan *plan, const void *act, uint32_t m, void *out,
+                                void *workspace, size_t workspace_bytes, uint32_t max_ctas, void *stream);
+
 /* qhtp_matmul_run without a caller workspace.  No counterpart in the reference.
  * For callers that may not allocate device memory when they run the op -- e.g. an inference-runtime
  * plugin called from the runtime's execute step, where the runtime owns and pre-plans every device

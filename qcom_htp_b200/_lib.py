@@ -74,6 +74,8 @@ SIGNATURES = {
     "qhtp_matmul_workspace_bytes": (C.c_size_t, [C.POINTER(QhtpMatmulPlan), C.c_uint32]),
     "qhtp_matmul_run": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                   C.c_size_t, C.c_void_p]),
+    "qhtp_matmul_run_ctas": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                                       C.c_size_t, C.c_uint32, C.c_void_p]),
     "qhtp_matmul_run_noalloc": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_void_p, C.c_uint32, C.c_void_p,
                                           C.c_void_p]),
     "qhtp_matmul_noalloc_check": (C.c_int, [C.POINTER(QhtpMatmulPlan), C.c_uint32, C.POINTER(C.c_int),

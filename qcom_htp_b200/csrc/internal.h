@@ -61,6 +61,7 @@ struct GemmLaunch {
   uint8_t* planes;        // workspace: u16 act byte planes [2][M][K] (A16 only)
   int* err;               // workspace: device error word
   cudaStream_t stream;
+  uint32_t max_ctas = 0;  // row-tiled GEMM: at most this many persistent CTAs (0: one per SM)
 };
 
 // qhtp_abi.cu: status of a CUDA result (records the error for qhtp_last_error_string), and a

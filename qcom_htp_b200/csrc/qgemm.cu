@@ -610,7 +610,9 @@ static cudaError_t launch_variant(const GemmLaunch& g, const CUtensorMap& ta, co
     attr_done = true;
   }
   const int total = prm.m_tiles * prm.n_tiles;
-  const int grid = total < sm_count() ? total : sm_count();
+  int slots = sm_count();
+  if (g.max_ctas != 0 && static_cast<int>(g.max_ctas) < slots) slots = static_cast<int>(g.max_ctas);
+  const int grid = total < slots ? total : slots;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);

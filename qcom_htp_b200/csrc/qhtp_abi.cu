@@ -254,6 +254,11 @@ size_t qhtp_matmul_workspace_bytes(const QhtpMatmulPlan* plan, uint32_t m) {
 
 QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan* plan, const void* act, uint32_t m, void* out, void* workspace,
                            size_t workspace_bytes, void* stream) {
+  return qhtp_matmul_run_ctas(plan, act, m, out, workspace, workspace_bytes, 0, stream);
+}
+
+QhtpStatus qhtp_matmul_run_ctas(const QhtpMatmulPlan* plan, const void* act, uint32_t m, void* out, void* workspace,
+                                size_t workspace_bytes, uint32_t max_ctas, void* stream) {
   if (!plan_ok(plan) || plan->prepared == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
   if (act == nullptr || out == nullptr || workspace == nullptr || m == 0) return QHTP_STATUS_INVALID_ARGUMENT;
   if (!aligned(act, 16) || !aligned(out, 16) || !aligned(workspace, 256)) return QHTP_STATUS_INVALID_ARGUMENT;
@@ -267,6 +272,7 @@ QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan* plan, const void* act, uint32_t
   g.planes = static_cast<uint8_t*>(workspace);
   g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, m));
   g.stream = as_stream(stream);
+  g.max_ctas = max_ctas;
   return from_cuda(launch_gemm(g));
 }
 

@@ -135,7 +135,9 @@ class QuantMatMul:
             self._ws[m] = ws
         return ws
 
-    def __call__(self, act: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    def __call__(self, act: torch.Tensor, out: torch.Tensor | None = None, stream=None, max_ctas: int = 0) -> torch.Tensor:
+        """out[M, N] = the quantized MatMul of act[M, K].  max_ctas > 0 limits the row-tiled GEMM to that
+        many SMs (qhtp_matmul_run_ctas), leaving the rest to concurrent work on other streams."""
         if act.dim() != 2 or act.shape[1] != self.k:
             raise ValueError(f"act must be [M, {self.k}]")
         if act.dtype != _dt(self.act_bits) or not act.is_cuda or not act.is_contiguous():
@@ -146,8 +148,8 @@ class QuantMatMul:
         elif out.shape != (m, self.n) or out.dtype != _dt(self.out_bits) or not out.is_contiguous():
             raise ValueError("bad output tensor")
         ws = self.workspace(m)
-        L.check("qhtp_matmul_run", L.lib.qhtp_matmul_run(
-            C.byref(self.plan), _ptr(act), m, _ptr(out), _ptr(ws), ws.numel(), _stream_handle(stream)))
+        L.check("qhtp_matmul_run", L.lib.qhtp_matmul_run_ctas(
+            C.byref(self.plan), _ptr(act), m, _ptr(out), _ptr(ws), ws.numel(), max_ctas, _stream_handle(stream)))
         return out
 
     def run_host(self, act_host: torch.Tensor, out_host: torch.Tensor | None = None, chunk_rows: int = 0,

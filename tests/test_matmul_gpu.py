@@ -138,3 +138,16 @@ def test_large_shape_properties_w4a16_lpbq():
     sub = O.QuantCase(c.family, c.act_q[rows], c.weight_q, c.weight_scale, c.bias_q, c.act_scale, c.out_scale,
                       c.lpbq_factor, c.lpbq_expanded)
     np.testing.assert_array_equal(out1.cpu().numpy()[rows], O.exact_output(sub))
+
+
+@pytest.mark.parametrize("max_ctas", [1, 16, 147])
+def test_run_on_fewer_sms_same_bytes(max_ctas):
+    """qhtp_matmul_run_ctas: the row-tiled GEMM on a limited number of SMs gives the same bytes."""
+    c = O.make_baseline_case("w4a16_lpbq", 512, 1024, 2048, seed=91)
+    op = build_op(c)
+    act = to_dev(c.act_q)
+    full = op(act)
+    part = op(act, max_ctas=max_ctas)
+    op.check_device(512)
+    assert torch.equal(full, part)
+    np.testing.assert_array_equal(part.cpu().numpy(), O.exact_output(c))
