@@ -3,16 +3,19 @@
 // fused into one kernel: the requantized output of a step is written straight into shared memory as
 // the next step's activation operand, so the intermediate results never reach HBM.
 //
-// Shape: K == N <= 256 (one or two 128-channel tiles; the reference's chain gates run at 256^3),
-// any M.  Output rows are independent across the chain, so every 128-row block is its own
-// thread-block cluster of n_tiles CTAs, CTA t owning output channels [128 t, 128 t + 128):
-//   * the CTA's weight planes (all of K) and channel records stay resident in shared memory;
-//   * each step: one thread issues the tcgen05 kind::i8 MMAs over K (accumulators in TMEM, the
-//     same operand images and TMEM layout as qgemm_kernel), all 8 warps drain TMEM, requantize with
-//     the exact epilogue of qgemm_kernel, and write the codes as the K block t of the next step's
-//     activation image (u16: split into the hi and lo byte planes), into this CTA's shared memory and
-//     through distributed shared memory into the peer CTA's; a cluster barrier publishes them;
+// Shape: K == N <= 256 (the reference's chain gates run at 256^3), any M.  Output rows are
+// independent across the chain, so every 128-row block is its own thread-block cluster of
+// ceil(N / 64) CTAs, CTA r owning output channels [64 r, 64 r + 64):
+//   * the CTA's rows of the weight image (its 64 channels' q and e' rows -- or hi and lo bytes -- for
+//     all of K) and its channel records stay resident in shared memory;
+//   * each step: one thread issues the tcgen05 kind::i8 MMAs over K (N = 128: [q | e'] of the 64
+//     channels), all 8 warps drain TMEM, requantize with the exact epilogue of qgemm_kernel (32
+//     channels per thread), and write the codes as bytes [64 r, 64 r + 64) of every row of the next
+//     step's activation image (u16: split into the hi and lo byte planes), into this CTA's shared
+//     memory and through distributed shared memory into every other CTA's of the cluster; a cluster
+//     barrier publishes them;
 //   * the last step stores the codes to global memory.
+// The requant work of a step, which bounds the kernel, is spread over N / 64 SMs per row block.
 // Activation images are double-buffered: step s reads buffer s & 1 and writes buffer (s + 1) & 1.  A
 // CTA writes a peer's buffer only after the cluster barrier that ends the previous step, which the
 // peer reaches after its MMAs of that step completed, so no MMA still reads a buffer being written.
@@ -28,7 +31,9 @@
 namespace qhtp {
 namespace {
 
-constexpr int kChainThreads = 256;  // 8 warps: warp w drains TMEM lane quadrant w % 4, channels 64*(w/4)..
+constexpr int kChainThreads = 256;  // 8 warps: warp w drains TMEM lane quadrant w % 4, channels 32*(w/4)..
+constexpr int kChainCh = 64;        // output channels per CTA
+constexpr int kChainMaxCtas = 4;    // K == N <= 256
 constexpr int kActBlock = kTileM * kTileK;  // 16 KB: one 128-row x 128-byte K block of one byte plane
 
 struct ChainParams {
@@ -43,33 +48,21 @@ struct ChainParams {
 
 template <int PA, int MODE>
 struct ChainCfg {
-  static constexpr int kBRows = MODE == kModeExact ? 128 : 256;
-  static constexpr int kWBlock = kBRows * kTileK;  // one K block of the weight image
+  static constexpr int kImgRows = MODE == kModeExact ? 128 : 256;  // rows of a tile's weight image
+  static constexpr int kBRows = MODE == kModeExact ? 64 : 128;     // this CTA's rows of it
+  static constexpr int kWBlock = kBRows * kTileK;                  // one K block of them
   static constexpr int kActBuf(int kb) { return PA * kb * kActBlock; }
 };
 
-// bytes of dynamic shared memory: weights + two activation images + records + barriers; at least
-// 120 KB so that one CTA occupies an SM (the TMEM allocation of 512 columns is then never contended
-// by a second CTA of this kernel)
+// Dynamic shared memory: weights + two activation images + records + barriers; at least 120 KB so
+// that one CTA occupies an SM (its TMEM allocation is then never contended by a second CTA of this
+// kernel).
 template <int PA, int MODE>
 constexpr int chain_smem_bytes(int kb) {
-  const int b = kb * ChainCfg<PA, MODE>::kWBlock + 2 * ChainCfg<PA, MODE>::kActBuf(kb) + kTileN * 32 + 64 + 1024;
+  const int b = kb * ChainCfg<PA, MODE>::kWBlock + 2 * ChainCfg<PA, MODE>::kActBuf(kb) + kChainCh * 32 + 64 + 1024;
   return b < 120 * 1024 ? 120 * 1024 : b;
 }
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t map_peer(uint32_t local_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
-  return r;
-}
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
@@ -94,22 +87,24 @@ template <int PA, int MODE>
 __global__ void __launch_bounds__(kChainThreads, 1)
     qchain_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const ChainParams p) {
   using Cfg = ChainCfg<PA, MODE>;
-  const int KB = p.kblocks;  // == number of channel tiles == cluster size
+  const int KB = p.kblocks;                       // 128-byte K blocks (1 or 2)
+  const int NC = static_cast<int>(gridDim.x) / ((p.M + kTileM - 1) / kTileM);  // CTAs per cluster
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wimg = smem;                                     // [KB][kBRows][128]
   uint8_t* act = wimg + KB * Cfg::kWBlock;                  // [2][PA][KB][128][128]
   ChannelRecord* rec_s = reinterpret_cast<ChannelRecord*>(act + 2 * Cfg::kActBuf(KB));
-  uint64_t* load_bar = reinterpret_cast<uint64_t*>(rec_s + kTileN);
+  uint64_t* load_bar = reinterpret_cast<uint64_t*>(rec_s + kChainCh);
   uint64_t* mma_bar = load_bar + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t ct = cluster_rank();                       // this CTA's channel tile
-  const int rb = blockIdx.x / KB;                           // 128-row block
+  const uint32_t rank = cluster_ctarank();        // this CTA's 64-channel slice
+  const int rb = blockIdx.x / NC;                 // 128-row block
   const int quad = warp & 3, half = warp >> 2;
-  const int row = quad * 32 + lane;                         // TMEM lane = output row in the block
+  const int row = quad * 32 + lane;               // TMEM lane = output row in the block
   const int m = rb * kTileM + row;
+  const int tile = static_cast<int>(rank) >> 1, hsel = static_cast<int>(rank) & 1;  // image tile, its half
 
   if (threadIdx.x == 0) {
     mbar_init(load_bar, 1);
@@ -117,14 +112,14 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(tslot, 512);
+    tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
-  // this tile's channel records (4 KB) into shared memory
-  for (int i = threadIdx.x; i < kTileN * 2; i += kChainThreads)
-    reinterpret_cast<uint4*>(rec_s)[i] = __ldg(reinterpret_cast<const uint4*>(p.rec + ct * kTileN) + i);
+  // this slice's 64 channel records (2 KB) into shared memory
+  for (int i = threadIdx.x; i < kChainCh * 2; i += kChainThreads)
+    reinterpret_cast<uint4*>(rec_s)[i] = __ldg(reinterpret_cast<const uint4*>(p.rec + rank * kChainCh) + i);
   tc_fence_before();
-  cluster_sync();  // barriers initialised, TMEM allocated, every CTA of the cluster running
+  cluster_sync_all();  // barriers initialised, TMEM allocated, every CTA of the cluster running
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
@@ -134,7 +129,10 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     tma_prefetch_desc(&tmB);
     mbar_arrive_expect_tx(load_bar, KB * Cfg::kWBlock + PA * KB * kActBlock);
     for (int kb = 0; kb < KB; ++kb) {
-      tma_load_2d(wimg + kb * Cfg::kWBlock, &tmB, load_bar, 0, (ct * KB + kb) * Cfg::kBRows);
+      const int img = (tile * KB + kb) * Cfg::kImgRows + 64 * hsel;  // first row of this slice's q rows
+      tma_load_2d(wimg + kb * Cfg::kWBlock, &tmB, load_bar, 0, img);
+      if constexpr (Cfg::kBRows == 128)  // the e' (or lo-byte) rows of the same channels
+        tma_load_2d(wimg + kb * Cfg::kWBlock + 64 * kTileK, &tmB, load_bar, 0, img + 128);
       for (int pl = 0; pl < PA; ++pl)
         tma_load_2d(act + (pl * KB + kb) * kActBlock, &tmA, load_bar, kb * kTileK, pl * p.a_plane_rows + rb * kTileM);
     }
@@ -142,8 +140,9 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   }
 
   const bool u16 = p.qmax > 255;
-  const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
-  const uint32_t peer = ct ^ 1u;
+  const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  // the byte column of this slice's channels in the next activation's rows
+  const int kb_out = static_cast<int>(rank) >> 1, col_out = 64 * (static_cast<int>(rank) & 1);
   for (int step = 0; step < p.chain; ++step) {
     const int bin = step & 1;
     // ---------------------------------------------------------------- MMAs of this step (one thread)
@@ -160,15 +159,15 @@ __global__ void __launch_bounds__(kChainThreads, 1)
             const uint32_t acc = (kb | kk) ? 1u : 0u;
             const uint64_t ko = static_cast<uint64_t>(kk * 2);
             if constexpr (MODE == kModeW16) {
-              constexpr uint32_t idS = idesc_i8(128, 128, 0, 1);
-              constexpr uint32_t idU = idesc_i8(128, 128, 0, 0);
-              const uint64_t dBhi = dB + ko, dBlo = dB + ko + (128 * kTileK >> 4);
+              constexpr uint32_t idS = idesc_i8(128, 64, 0, 1);
+              constexpr uint32_t idU = idesc_i8(128, 64, 0, 0);
+              const uint64_t dBhi = dB + ko, dBlo = dB + ko + (64 * kTileK >> 4);
               mma_i8(tmem + 0, dA0 + ko, dBhi, idS, acc);
-              mma_i8(tmem + 128, dA0 + ko, dBlo, idU, acc);
-              mma_i8(tmem + 128, dA1 + ko, dBhi, idS, 1u);
-              mma_i8(tmem + 256, dA1 + ko, dBlo, idU, acc);
+              mma_i8(tmem + 64, dA0 + ko, dBlo, idU, acc);
+              mma_i8(tmem + 64, dA1 + ko, dBhi, idS, 1u);
+              mma_i8(tmem + 128, dA1 + ko, dBlo, idU, acc);
             } else {
-              constexpr int N = Cfg::kBRows;
+              constexpr int N = Cfg::kBRows;  // 128 = [q | e'] of 64 channels (f32 mode), 64 = q (exact mode)
               constexpr uint32_t id = idesc_i8(128, N, 0, 1);
               mma_i8(tmem + 0, dA0 + ko, dB + ko, id, acc);
               if constexpr (PA == 2) mma_i8(tmem + N, dA1 + ko, dB + ko, id, acc);
@@ -179,28 +178,28 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       mma_commit(mma_bar);
     }
     // ---------------------------------------------------------------- epilogue (all 8 warps)
-    const bool got = mbar_wait(mma_bar, step & 1, p.err, kErrTimeoutAccum);
+    mbar_wait(mma_bar, step & 1, p.err, kErrTimeoutAccum);
     tc_fence_after();
     const bool last = step == p.chain - 1;
     const uint32_t obase = smem_u32(act + (bin ^ 1) * Cfg::kActBuf(KB));
 #pragma unroll 1
-    for (int g = 0; g < 4; ++g) {
-      const int c0 = half * 64 + g * 16;  // first of this group's 16 channels within the tile
+    for (int g = 0; g < 2; ++g) {
+      const int c0 = half * 32 + g * 16;  // first of this group's 16 channels within the slice
       int64_t T[16];
       {
         uint32_t a0[16], a1[16], a2[16], a3[16];
-        tmem_ld16(tl + g * 16, a0);
+        tmem_ld16(tl + c0, a0);
         if constexpr (MODE == kModeF32) {
-          tmem_ld16(tl + g * 16 + 128, a1);
+          tmem_ld16(tl + c0 + 64, a1);
           if constexpr (PA == 2) {
-            tmem_ld16(tl + g * 16 + 256, a2);
-            tmem_ld16(tl + g * 16 + 384, a3);
+            tmem_ld16(tl + c0 + 128, a2);
+            tmem_ld16(tl + c0 + 192, a3);
           }
         } else if constexpr (MODE == kModeW16) {
-          tmem_ld16(tl + g * 16 + 128, a1);
-          tmem_ld16(tl + g * 16 + 256, a2);
+          tmem_ld16(tl + c0 + 64, a1);
+          tmem_ld16(tl + c0 + 128, a2);
         } else if constexpr (PA == 2) {
-          tmem_ld16(tl + g * 16 + 128, a1);
+          tmem_ld16(tl + c0 + 64, a1);
         }
         tmem_ld_wait();
 #pragma unroll
@@ -224,7 +223,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         }
       }
       uint32_t code[16];
-      const bool real = ct * kTileN + c0 < p.N;  // 16-channel groups lie wholly inside or past N
+      const int n_first = static_cast<int>(rank) * kChainCh + c0;
+      const bool real = n_first < p.N;  // 16-channel groups lie wholly inside or past N (N % 32 == 0)
       if (real) {
         uint32_t near_mask = 0;
         int64_t wv[16];
@@ -253,8 +253,10 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         for (int j = 0; j < 16; ++j) code[j] = 0;
       }
       if (!last) {
-        // next activation: K block ct, bytes c0..c0+15 of row `row` (one swizzled 16-byte chunk)
-        const uint32_t chunk = static_cast<uint32_t>(row * kTileK + ((((c0 >> 4) ^ row) & 7) << 4));
+        // next activation: K block kb_out, bytes col_out + c0 .. +15 of row `row` (one swizzled
+        // 16-byte chunk), here and in every other CTA of the cluster
+        const int chunk = (col_out + c0) >> 4;
+        const uint32_t off = static_cast<uint32_t>(kb_out * kActBlock + row * kTileK + (((chunk ^ row) & 7) << 4));
         uint32_t hb[16], lb[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -262,17 +264,19 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           lb[j] = code[j] & 0xFFu;
         }
         const uint4 vh = pack16(hb);
-        const uint32_t a_hi = obase + ct * kActBlock + chunk;
+        const uint32_t a_hi = obase + off;
         st_shared_v4(a_hi, vh);
-        if (KB == 2) st_cluster_v4(map_peer(a_hi, peer), vh);
+        for (int r = 0; r < NC; ++r)
+          if (r != static_cast<int>(rank)) st_cluster_v4(mapa_shared(a_hi, static_cast<uint32_t>(r)), vh);
         if constexpr (PA == 2) {
           const uint4 vl = pack16(lb);
-          const uint32_t a_lo = obase + (KB + ct) * kActBlock + chunk;
+          const uint32_t a_lo = obase + KB * kActBlock + off;
           st_shared_v4(a_lo, vl);
-          if (KB == 2) st_cluster_v4(map_peer(a_lo, peer), vl);
+          for (int r = 0; r < NC; ++r)
+            if (r != static_cast<int>(rank)) st_cluster_v4(mapa_shared(a_lo, static_cast<uint32_t>(r)), vl);
         }
       } else if (real && m < p.M) {
-        const size_t o = static_cast<size_t>(m) * p.N + ct * kTileN + c0;
+        const size_t o = static_cast<size_t>(m) * p.N + n_first;
         if (u16) {
           uint4 v0, v1;
           v0.x = code[0] | (code[1] << 16);
@@ -294,32 +298,31 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         }
       }
     }
-    (void)got;
-    // every TMEM read of this step is done and the next activation is in place (both CTAs): the
+    // every TMEM read of this step is done and the next activation is in place (every CTA): the
     // generic-proxy shared-memory writes are made visible to the tensor core's async proxy
     tc_fence_before();
     asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
-    cluster_sync();
+    cluster_sync_all();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 512);
+  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 template <int PA, int MODE>
 cudaError_t launch_chain_variant(const CUtensorMap& ta, const CUtensorMap& tb, const ChainParams& prm, int m_blocks,
-                                 cudaStream_t stream) {
+                                 int ctas, cudaStream_t stream) {
   const int smem = chain_smem_bytes<PA, MODE>(prm.kblocks);
   cudaError_t e = cudaFuncSetAttribute(qchain_kernel<PA, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(m_blocks * prm.kblocks), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(m_blocks * ctas), 1, 1);
   cfg.blockDim = dim3(kChainThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(prm.kblocks);
+  attr[0].val.clusterDim.x = static_cast<unsigned>(ctas);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
@@ -330,7 +333,7 @@ cudaError_t launch_chain_variant(const CUtensorMap& ta, const CUtensorMap& tb, c
 }  // namespace
 
 bool chain_fusable(const QhtpMatmulPlan* pl) {
-  return pl->mode != kModeGroup && pl->k == pl->n && pl->n <= 2 * kTileN && pl->act_bits == pl->out_bits &&
+  return pl->mode != kModeGroup && pl->k == pl->n && pl->n <= kChainMaxCtas * kChainCh && pl->act_bits == pl->out_bits &&
          pl->k_pad / kTileK == pl->n_tiles;
 }
 
@@ -351,7 +354,11 @@ cudaError_t launch_chain(const GemmLaunch& g, uint32_t chain) {
   }
   CUtensorMap ta, tb;
   if (!make_tmap_2d_u8(&ta, a_base, K, a_rows, K, kTileK, kTileM)) return cudaErrorInvalidValue;
-  if (!make_tmap_planes(&tb, pl)) return cudaErrorInvalidValue;
+  // the weight images as 64-row boxes: one CTA's q (or hi-byte) rows, then its e' (or lo-byte) rows
+  const uint64_t img_rows = static_cast<uint64_t>(pl->n_tiles) * (pl->k_pad / kTileK) * b_rows_for_mode(pl->mode);
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl->prepared, kTileK, img_rows, kTileK, kTileK, 64,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
   ChainParams prm;
   prm.M = static_cast<int>(g.m);
   prm.N = static_cast<int>(pl->n);
@@ -368,12 +375,13 @@ cudaError_t launch_chain(const GemmLaunch& g, uint32_t chain) {
   prm.out_exp2 = pl->out_exp2;
   prm.err = g.err;
   const int m_blocks = static_cast<int>((g.m + kTileM - 1) / kTileM);
+  const int ctas = static_cast<int>((pl->n + kChainCh - 1) / kChainCh);
   switch (pl->mode * 2 + (pl->a_planes - 1)) {
-    case kModeF32 * 2 + 0: return launch_chain_variant<1, kModeF32>(ta, tb, prm, m_blocks, g.stream);
-    case kModeF32 * 2 + 1: return launch_chain_variant<2, kModeF32>(ta, tb, prm, m_blocks, g.stream);
-    case kModeExact * 2 + 0: return launch_chain_variant<1, kModeExact>(ta, tb, prm, m_blocks, g.stream);
-    case kModeExact * 2 + 1: return launch_chain_variant<2, kModeExact>(ta, tb, prm, m_blocks, g.stream);
-    case kModeW16 * 2 + 1: return launch_chain_variant<2, kModeW16>(ta, tb, prm, m_blocks, g.stream);
+    case kModeF32 * 2 + 0: return launch_chain_variant<1, kModeF32>(ta, tb, prm, m_blocks, ctas, g.stream);
+    case kModeF32 * 2 + 1: return launch_chain_variant<2, kModeF32>(ta, tb, prm, m_blocks, ctas, g.stream);
+    case kModeExact * 2 + 0: return launch_chain_variant<1, kModeExact>(ta, tb, prm, m_blocks, ctas, g.stream);
+    case kModeExact * 2 + 1: return launch_chain_variant<2, kModeExact>(ta, tb, prm, m_blocks, ctas, g.stream);
+    case kModeW16 * 2 + 1: return launch_chain_variant<2, kModeW16>(ta, tb, prm, m_blocks, ctas, g.stream);
     default: return cudaErrorInvalidValue;
   }
 }

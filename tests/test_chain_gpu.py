@@ -69,9 +69,10 @@ def test_chain_ragged_rows(family, m):
 
 
 @pytest.mark.parametrize("family", ["w4a8_per_channel", "w4a16_per_channel"])
-@pytest.mark.parametrize("kn", [32, 128, 192])
+@pytest.mark.parametrize("kn", [32, 96, 128, 192])
 def test_chain_one_tile_and_partial_tile(family, kn):
-    """K == N = 32 / 128: one channel tile (a cluster of one CTA); 192: the second tile half full."""
+    """Clusters of ceil(N / 64) CTAs, 64 channels each: N = 32 (one CTA, half full), 96 (two, the
+    second half full), 128 (two), 192 (three)."""
     c = O.generate_case(family, "normal_random", 130, kn, kn)
     op = build_op(c)
     np.testing.assert_array_equal(run_chain(op, c.act_q, kn, 8), oracle_chain(c, 8))
