@@ -962,7 +962,8 @@ def run_decode(args, world, rank, local, stream, shapes=None) -> list:
     """BASELINE decode/prefill rows of the W4A16 LPBQ GEMM (M in {1, 16, 128}, K = 4096,
     N in {4096, 14336}): HBM-bound.  Reports GB/s on the algorithmic bytes (int4 weights, block
     factors, scales, bias, u16 activation and output) and on the bytes the kernel reads (the
-    prepared byte planes: q and the float32-dequant residual e', 2 bytes per weight)."""
+    prepared byte planes: q and the float32-dequant residual e', 2 bytes per weight; or, for the
+    int4 code stream, 0.5 byte per weight plus factors and e' tables)."""
     dev = torch.device("cuda", local)
     pk = peaks()
     flush = L2Flush(dev)
@@ -978,14 +979,23 @@ def run_decode(args, world, rank, local, stream, shapes=None) -> list:
         op.check_device(m)
         t = max_over_ranks(statistics.mean(times), world)   # the event clock ticks in ~1 us steps
         alg = gemm_alg_bytes(d, n)
-        read = int(op.plan.plane_bytes) + n * 32 + m * k * 2 + m * n * 2
-        # the library's dispatch: the channel-major decode kernel up to 64 rows, and up to 128 rows
-        # when the channel tiles leave room for a K split; else the row-tiled GEMM
-        row_tiled = m > 64 and 2 * ((n + 127) // 128) > sms
+        # the library's dispatch: the int4 code stream for one or two rows over a long weight stream
+        # (>= 6 stages of 256 K per SM); the channel-major decode kernel up to 64 rows, and up to 128
+        # rows when the channel tiles leave room for a K split; else the row-tiled GEMM
+        n_tiles = (n + 127) // 128
+        code_stream = m <= 2 and bool(op.plan.flags & 2) and n_tiles * (k // 256) >= 6 * sms
+        row_tiled = m > 64 and 2 * n_tiles > sms
+        if code_stream:  # codes, factors per 32 K, one e' table set per tile, records, activation, output
+            read = n_tiles * 128 * k // 2 + n_tiles * (k // 32) * 128 + n_tiles * 16 * 128 * 16 + n * 32 + \
+                m * k * 2 + m * n * 2
+            kernel = "qgemv4_kernel (int4 code stream, CUDA cores) + dec4_combine_kernel"
+        else:
+            read = int(op.plan.plane_bytes) + n * 32 + m * k * 2 + m * n * 2
+            kernel = "split_u16_planes + " + ("qgemm_kernel (row tiles)" if row_tiled else
+                                              "qdecode_kernel (channel-major, cluster split-K)")
         chk = check_gemm_sample(d, out)
         rows.append({"m": m, "k": k, "n": n, "us": round(t * 1e6, 2),
-                     "kernel": "split_u16_planes + " + ("qgemm_kernel (row tiles)" if row_tiled else
-                                                        "qdecode_kernel (channel-major, cluster split-K)"),
+                     "kernel": kernel,
                      "alg_bytes": alg, "alg_gbs": round(alg / t / 1e9, 1),
                      "alg_frac": round(alg / t / 1e9 / pk["hbm_gbs"], 3),
                      "read_bytes": read, "read_gbs": round(read / t / 1e9, 1),

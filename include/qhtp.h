@@ -116,7 +116,7 @@ typedef struct QhtpMatmulPlan {
   double act_scale, out_scale;
   uint64_t act_mant;      /* act_scale = act_mant * 2^act_exp2, 53-bit mantissa */
   int32_t act_exp2;
-  uint32_t flags;         /* kernel options chosen by qhtp_matmul_prepare from the prepared weights */
+  uint32_t flags;         /* kernel options (QHTP_PLAN_FLAG_*); qhtp_matmul_prepare sets the first two */
   uint64_t out_mant;
   int32_t out_exp2;
   uint64_t plane_bytes;   /* prepared weight planes */
@@ -124,6 +124,16 @@ typedef struct QhtpMatmulPlan {
   uint64_t prepared_bytes;
   void *prepared;         /* device buffer bound by qhtp_matmul_prepare */
 } QhtpMatmulPlan;
+
+/* QhtpMatmulPlan.flags.  LO_RESIDUAL_BY_BOUND: the u16 row-tiled GEMM leaves the lo-plane x e' product
+ * out of its MMAs (bounded per channel, exact fix-up near rounding boundaries).  INT4_STREAM: the
+ * prepared buffer holds the 4-bit code image (int4 families, per-channel or LPBQ with factors in
+ * [1, 16], K % 256 == 0) and runs of M <= 2 rows over a long enough weight stream (at least six
+ * 256-deep stages per SM) read it instead of the byte planes.  FORCE_INT4_STREAM: set by the caller
+ * before or after prepare; M <= 2 then takes the code stream at any shape (tests, benchmarks). */
+#define QHTP_PLAN_FLAG_LO_RESIDUAL_BY_BOUND 1u
+#define QHTP_PLAN_FLAG_INT4_STREAM 2u
+#define QHTP_PLAN_FLAG_FORCE_INT4_STREAM 4u
 
 /* Validate shapes / family / schema and fill *plan (host only, no device access).
  * Requirements: K % 32 == 0, 32 <= K <= 32768, N % 32 == 0, N >= 32; LPBQ only for int4 families. */
@@ -133,8 +143,9 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights *w, QhtpMatmulPlan *plan);
 size_t qhtp_matmul_prepared_bytes(const QhtpMatmulPlan *plan);
 
 /* Build the prepared record in `prepared` (device, >= prepared_bytes, 256-byte aligned):
- * byte-plane weights in the tiled layout the kernel streams, and one 32-byte record per output
- * channel (effective bias, requant multiplier, exact-path exponents).  This is the B200 analogue
+ * byte-plane weights in the tiled layout the kernel streams, one 32-byte record per output
+ * channel (effective bias, requant multiplier, exact-path exponents) and, for the int4 families,
+ * the 4-bit code image with its per-(channel, factor) e' tables.  This is the B200 analogue
  * of the reference's prepare-time const-fold (HmxW4LpbqExpandToI8Op.cpp:107-157,
  * gen_quant_chain.py:879).  Synchronizes `stream` to validate the scales. */
 QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan *plan, const QhtpMatmulWeights *w, void *prepared,

@@ -16,7 +16,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libqhtp.so"
-SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "gdn256x2.cu", "noalloc.cu", "wire.cu", "gdn256f.cu", "qgroup.cu", "peak.cu", "qchain.cu"]
+SOURCES = ["qhtp_abi.cu", "qgemm.cu", "qdecode.cu", "gdn.cu", "gdn256.cu", "gdn256x2.cu", "noalloc.cu", "wire.cu", "gdn256f.cu", "qgroup.cu", "peak.cu", "qchain.cu", "qdec4.cu"]
 HEADERS = ["ptx.cuh", "requant.cuh", "internal.h", "gdn_common.cuh"]
 
 NVCC_FLAGS = [

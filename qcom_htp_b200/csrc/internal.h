@@ -24,6 +24,9 @@ constexpr uint32_t kPlanLoResidualByBound = 1u;  // the lo-plane x e' product is
                                                  // bounded per channel (ChannelRecord::lo_win); elements
                                                  // within that bound of a rounding boundary get it exactly
 constexpr int32_t kLoWinMax = 1 << 20;           // widest per-channel window that enables it (~1e-3 units)
+constexpr uint32_t kPlanInt4Stream = 2u;         // the int4 code image was built (qdec4.cu): decode rows
+                                                 // stream 4-bit codes instead of the byte planes
+constexpr uint32_t kPlanForceInt4Stream = 4u;    // set by the caller: M <= 2 takes the code stream at any shape
 constexpr int kSumsPerChannel = 4;               // prepare scratch: sum q, sum e', sum |e'|, unused
 
 constexpr int kTileM = 128;      // rows per CTA tile (TMEM lanes)
@@ -62,6 +65,7 @@ struct GemmLaunch {
   int* err;               // workspace: device error word
   cudaStream_t stream;
   uint32_t max_ctas = 0;  // row-tiled GEMM: at most this many persistent CTAs (0: one per SM)
+  uint8_t* dec4 = nullptr;  // workspace area of the int4-stream decode kernel (dec4_workspace_bytes)
 };
 
 // qhtp_abi.cu: status of a CUDA result (records the error for qhtp_last_error_string), and a
@@ -83,6 +87,20 @@ bool decode_supported(const QhtpMatmulPlan* plan, uint32_t m);
 cudaError_t launch_decode(const GemmLaunch& g, const uint8_t* a_base);
 cudaError_t launch_prepare(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
                            int* bad_scale, cudaStream_t stream);
+// qdec4.cu: decode rows (M <= kDec4MaxM) of int4-weight plans (per-channel or LPBQ, K % 256 == 0),
+// streaming the 4-bit codes; the prepared buffer holds its code image after the per-channel sums
+constexpr uint32_t kDec4MaxM = 2;
+bool int4_stream_layout(const QhtpMatmulPlan* plan);                 // the plan has the code image
+size_t int4_image_bytes(const QhtpMatmulPlan* plan);                 // 0 when it has none
+size_t int4_image_offset(const QhtpMatmulPlan* plan);                // in the prepared buffer
+size_t dec4_workspace_bytes(const QhtpMatmulPlan* plan, uint32_t m);  // 0 when the kernel cannot run
+bool dec4_supported(const QhtpMatmulPlan* plan, uint32_t m);         // prepared, flag set, m in range
+// status[2] != 0 after the stream completes: a block factor outside [1, 16] (the codes stay unused)
+cudaError_t launch_prepare_int4(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
+                                int* status, cudaStream_t stream);
+cudaError_t launch_dec4(const GemmLaunch& g);
+// qhtp_abi.cu: the int4-stream decode area inside a run's workspace (nullptr when it has none)
+uint8_t* dec4_area(const QhtpMatmulPlan* plan, uint32_t m, uint8_t* workspace);
 // qgroup.cu: the per-group W4 schema (prepare, and the GEMM on the u8 activation or byte planes)
 cudaError_t launch_prepare_group(const QhtpMatmulPlan* plan, const QhtpMatmulWeights* w, void* prepared,
                                  int* bad_scale, cudaStream_t stream, int sms);

@@ -87,6 +87,7 @@ extern "C" QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan* plan, const 
   g.out = out;
   g.planes = scratch;
   g.err = err;
+  g.dec4 = qhtp::dec4_area(plan, m, scratch);
   g.stream = s;
   return qhtp::status_from_cuda(qhtp::launch_gemm(g));
 }

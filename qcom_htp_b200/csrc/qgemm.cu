@@ -140,12 +140,6 @@ struct GemmCfg {
   static constexpr int kSmem = kStages * kStage + kRecBytes + 1024 + 256;
 };
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
 // Named barrier 1 over the epilogue warps, and the same barrier ANDing a predicate (every thread
 // leaves with the same answer, so a bounded wait that gave up anywhere stops all of them together).
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
@@ -641,6 +635,7 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   CUtensorMap ta, tb;
   const uint8_t* a_base;
   uint64_t a_rows;
+  if (g.dec4 != nullptr && dec4_supported(pl, g.m)) return launch_dec4(g);  // int4 codes, M <= 16
   if (pl->a_planes == 2) {
     const size_t total = static_cast<size_t>(g.m) * K;
     cudaError_t e = launch_split_u16(static_cast<const uint16_t*>(g.act), g.planes, total, g.stream);

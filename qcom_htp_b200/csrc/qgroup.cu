@@ -71,12 +71,6 @@ struct GroupParams {
   int* err;
 };
 
-__device__ __forceinline__ void tmem_ld8_g(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
 template <int PA>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_group_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
@@ -232,11 +226,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t qh[8], eh[8], ql[8], el[8];
-            tmem_ld8_g(tb + h * 8, qh);       // sum x(_hi) * q, rows 8h..
-            tmem_ld8_g(tb + 64 + h * 8, eh);  // sum x(_hi) * e'
+            tmem_ld8(tb + h * 8, qh);       // sum x(_hi) * q, rows 8h..
+            tmem_ld8(tb + 64 + h * 8, eh);  // sum x(_hi) * e'
             if constexpr (PA == 2) {
-              tmem_ld8_g(tb + 128 + h * 8, ql);  // sum x_lo * q
-              tmem_ld8_g(tb + 192 + h * 8, el);  // sum x_lo * e'
+              tmem_ld8(tb + 128 + h * 8, ql);  // sum x_lo * q
+              tmem_ld8(tb + 192 + h * 8, el);  // sum x_lo * e'
             }
             tmem_ld_wait();
             if (h == 1) {  // buffer b fully in registers: the next group's MMAs may overwrite it

@@ -50,7 +50,18 @@ size_t a16_plane_bytes(const QhtpMatmulPlan* p, uint32_t m) {
 
 bool plan_ok(const QhtpMatmulPlan* p) { return p != nullptr && p->magic == kPlanMagic; }
 
+// Workspace of a run over m rows: u16 byte planes | int4-stream decode area | 256-byte error area.
+size_t err_offset(const QhtpMatmulPlan* p, uint32_t m) { return a16_plane_bytes(p, m) + dec4_workspace_bytes(p, m); }
+
 }  // namespace
+
+namespace qhtp {
+
+uint8_t* dec4_area(const QhtpMatmulPlan* plan, uint32_t m, uint8_t* workspace) {
+  return dec4_workspace_bytes(plan, m) != 0 ? workspace + a16_plane_bytes(plan, m) : nullptr;
+}
+
+}  // namespace qhtp
 
 namespace qhtp {
 
@@ -211,8 +222,10 @@ QhtpStatus qhtp_matmul_plan(const QhtpMatmulWeights* w, QhtpMatmulPlan* plan) {
   // per-group: the (tile, group) constant blocks, then the float64 bias per channel
   p.record_bytes = p.mode == kModeGroup ? group_rec_bytes(&p) + align_up(npad * sizeof(double), 256)
                                         : align_up(npad * sizeof(ChannelRecord), 256);
-  // planes | records | per-channel sums (prepare scratch) | 256-byte status word area
-  p.prepared_bytes = p.plane_bytes + p.record_bytes + align_up(npad * 8 * kSumsPerChannel, 256) + 256;
+  // planes | records | per-channel sums (prepare scratch) | int4 code image (int4 families) |
+  // 256-byte status word area
+  p.prepared_bytes =
+      p.plane_bytes + p.record_bytes + align_up(npad * 8 * kSumsPerChannel, 256) + int4_image_bytes(&p) + 256;
   p.prepared = nullptr;
   *plan = p;
   return QHTP_STATUS_OK;
@@ -234,22 +247,25 @@ QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan* plan, const QhtpMatmulWeights* w,
   // status word: last 256-byte area of the prepared buffer (zeroed by the prepare memset)
   int* dflag = reinterpret_cast<int*>(static_cast<uint8_t*>(prepared) + plan->prepared_bytes - 256);
   cudaError_t e = launch_prepare(plan, w, prepared, dflag, s);
+  if (e == cudaSuccess) e = launch_prepare_int4(plan, w, prepared, dflag, s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
-  int h[2] = {0, 0};  // [0] bad-scale flag, [1] widest per-channel lo-plane residual window
+  // [0] bad-scale flag, [1] widest per-channel lo-plane residual window, [2] LPBQ factor outside [1, 16]
+  int h[3] = {0, 0, 0};
   e = cudaMemcpyAsync(h, dflag, sizeof(h), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
   if (h[0] != 0) return QHTP_STATUS_INVALID_ARGUMENT;  // a scale was zero, negative, subnormal or not finite
-  plan->flags = 0;
+  plan->flags &= kPlanForceInt4Stream;  // the caller's dispatch override survives a re-prepare
   if (plan->mode == kModeF32 && plan->a_planes == 2 && h[1] > 0 && h[1] <= kLoWinMax)
     plan->flags |= kPlanLoResidualByBound;
+  if (int4_stream_layout(plan) && h[2] == 0) plan->flags |= kPlanInt4Stream;
   plan->prepared = prepared;
   return QHTP_STATUS_OK;
 }
 
 size_t qhtp_matmul_workspace_bytes(const QhtpMatmulPlan* plan, uint32_t m) {
   if (!plan_ok(plan)) return 0;
-  return a16_plane_bytes(plan, m) + 256;
+  return err_offset(plan, m) + 256;
 }
 
 QhtpStatus qhtp_matmul_run(const QhtpMatmulPlan* plan, const void* act, uint32_t m, void* out, void* workspace,
@@ -270,7 +286,8 @@ QhtpStatus qhtp_matmul_run_ctas(const QhtpMatmulPlan* plan, const void* act, uin
   g.m = m;
   g.out = out;
   g.planes = static_cast<uint8_t*>(workspace);
-  g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, m));
+  g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + err_offset(plan, m));
+  g.dec4 = dec4_area(plan, m, static_cast<uint8_t*>(workspace));
   g.stream = as_stream(stream);
   g.max_ctas = max_ctas;
   return from_cuda(launch_gemm(g));
@@ -304,7 +321,7 @@ QhtpStatus qhtp_matmul_run_host(const QhtpMatmulPlan* plan, const void* act_host
   GemmLaunch g;
   g.plan = plan;
   g.planes = static_cast<uint8_t*>(workspace);
-  g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, rows));
+  g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + err_offset(plan, rows));
   g.stream = s;
   const uint32_t chunks = (m + rows - 1) / rows;
   for (uint32_t c = 0; c < chunks && e == cudaSuccess; ++c) {
@@ -320,6 +337,7 @@ QhtpStatus qhtp_matmul_run_host(const QhtpMatmulPlan* plan, const void* act_host
       g.act = a_d;
       g.m = rc;
       g.out = o_d;
+      g.dec4 = dec4_area(plan, rc, static_cast<uint8_t*>(workspace));
       e = launch_gemm(g);
     }
     if (e == cudaSuccess) e = cudaEventRecord(hp->computed[c], s);
@@ -338,7 +356,7 @@ QhtpStatus qhtp_matmul_check(const QhtpMatmulPlan* plan, void* workspace, uint32
                              void* stream) {
   if (!plan_ok(plan) || workspace == nullptr) return QHTP_STATUS_INVALID_ARGUMENT;
   cudaStream_t s = as_stream(stream);
-  int* err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + a16_plane_bytes(plan, m));
+  int* err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + err_offset(plan, m));
   int h = 0;
   cudaError_t e = cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(int), s);
@@ -412,7 +430,7 @@ QhtpStatus run_prepared(const QhtpPreparedRun* run, uint32_t family) {
     g.m = run->m;
     g.out = run->output.data;
     g.planes = static_cast<uint8_t*>(run->scratch.data);
-    g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(run->scratch.data) + a16_plane_bytes(pl, run->m));
+    g.err = reinterpret_cast<int*>(static_cast<uint8_t*>(run->scratch.data) + err_offset(pl, run->m));
     g.stream = as_stream(run->stream);
     return from_cuda(launch_chain(g, run->chain));
   }

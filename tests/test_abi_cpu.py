@@ -54,6 +54,25 @@ def test_plan_valid_shapes(L):
     assert Fraction(p.act_mant) * Fraction(2) ** p.act_exp2 == Fraction(1e-4)
 
 
+def test_plan_int4_code_image_and_decode_workspace(L):
+    """int4 families also carry the 4-bit code image (0.5 B per weight, one factor byte per 32
+    weights, 16 e' tables of 16 B per channel); runs of M <= 2 rows reserve the partial-sum slots of
+    the code-stream kernel (160 CTAs x 2 segments x M x 128 channels x 8 B) before the error word."""
+    p = L.QhtpMatmulPlan()
+    assert L.lib.qhtp_matmul_plan(C.byref(_weights(L)), C.byref(p)) == L.OK
+    image = 112 * 128 * 4096 // 2 + 112 * (4096 // 32) * 128 + 112 * 16 * 128 * 16
+    assert p.prepared_bytes >= 112 * 256 * 4096 + 112 * 128 * 32 + image
+    ws = [L.lib.qhtp_matmul_workspace_bytes(C.byref(p), m) for m in (1, 2, 3)]
+    assert ws[0] >= 2 * 4096 + 160 * 2 * 1 * 128 * 8 + 256
+    assert ws[1] >= 4 * 4096 + 160 * 2 * 2 * 128 * 8 + 256
+    assert ws[2] == -(-6 * 4096 // 256) * 256 + 256  # M = 3: byte planes and the error word only
+    # an 8-bit family has no code image
+    q = L.QhtpMatmulPlan()
+    assert L.lib.qhtp_matmul_plan(C.byref(_weights(L, family=L.FAMILY["w8a16"], schema=L.SCHEMA["per_channel"],
+                                                   lpbq_block=0, lpbq_block_scale=None)), C.byref(q)) == L.OK
+    assert L.lib.qhtp_matmul_workspace_bytes(C.byref(q), 1) == 2 * 4096 + 256
+
+
 @pytest.mark.parametrize("kw,status", [
     (dict(k=4000), 2), (dict(n=100), 2), (dict(k=0), 1), (dict(family=9), 1), (dict(schema=5), 1),
     (dict(lpbq_block=48), 2), (dict(lpbq_block=4096), 2), (dict(act_scale=0.0), 1), (dict(out_scale=-1.0), 1),
