@@ -175,7 +175,7 @@ QhtpStatus qhtp_matmul_run_ctas(const QhtpMatmulPlan *plan, const void *act, uin
  * The u16 activation planes and the error word live in a fixed area inside the library
  * (QHTP_NOALLOC_SCRATCH_BYTES of device memory, held by every GPU that loads the library until the
  * process exits), so M*K is limited: the call needs qhtp_matmul_workspace_bytes(plan, m) <=
- * QHTP_NOALLOC_SCRATCH_BYTES (for u16 activations 2*M*K + 256 bytes; u8 activations need only 256)
+ * QHTP_NOALLOC_SCRATCH_BYTES (u16 byte planes, int4 decode partials for M <= 2, the error word)
  * and returns QHTP_STATUS_INVALID_ARGUMENT with a qhtp_last_error_string message otherwise.  The
  * first call on each device looks up the area's device address: make it before any stream capture.
  * All calls share the area: calls whose work overlaps on the GPU race, so serialize them.  Calls no

@@ -65,11 +65,11 @@ extern "C" QhtpStatus qhtp_matmul_run_noalloc(const QhtpMatmulPlan* plan, const 
   if (reinterpret_cast<uintptr_t>(act) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return QHTP_STATUS_INVALID_ARGUMENT;
   if (m > (1u << 24)) return QHTP_STATUS_UNSUPPORTED;  // the row limit of qhtp_matmul_run
-  const size_t need = qhtp_matmul_workspace_bytes(plan, m);  // u16 byte planes + 256-byte error area
+  const size_t need = qhtp_matmul_workspace_bytes(plan, m);  // run workspace, error word last
   if (need == 0 || need > kScratchBytes) {
     qhtp::set_last_message(
         "qhtp_matmul_run_noalloc: qhtp_matmul_workspace_bytes(plan, M) exceeds the library's fixed 8 MiB "
-        "scratch (u16 activations need align_up(2*M*K, 256) + 256 bytes); use qhtp_matmul_run with a "
+        "scratch; use qhtp_matmul_run with a "
         "caller workspace");
     return QHTP_STATUS_INVALID_ARGUMENT;
   }
