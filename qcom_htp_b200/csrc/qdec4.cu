@@ -332,19 +332,19 @@ __device__ __forceinline__ int d4_owner(int u, const D4Params& p) { return ((u +
 __device__ __forceinline__ uint32_t pick(uint32_t n, uint32_t p, uint32_t m) { return (n & ~m) | (p & m); }
 
 // e' bytes of one code word (8 weights, nibble i = K position i, offset binary u) by 16-entry table
-// lookup: byte u of the table is e' for code u; prmt on the code selects from the table's first half
-// (u < 8), prmt on code ^ 8 from its second half, and the bit-3 mask (prmt in sign-replicate mode
-// over the code shifted into each byte's sign bit) picks between them.  K positions 0..3 | 4..7.
-// The shifts run on the multiply pipe (w * 16 and the high word of w * 2^16), the permutes and
-// selects on the integer pipe.
+// lookup: byte u of the table is e' for code u.  With the code's bit 3 cleared (u & 7, every
+// selector nibble in plain byte-select mode), one prmt reads the table's first half (entries 0..7)
+// and one its second half (8..15); the bit-3 mask (prmt in sign-replicate mode over the code shifted
+// into each byte's sign bit) picks between them.  K positions 0..3 | 4..7.  The shifts run on the
+// multiply pipe (w * 16 and the high word of w7 * 2^16), the permutes and selects on the integer pipe.
 __device__ __forceinline__ void d4_lookup(uint32_t w, const uint4& et, uint32_t& e0, uint32_t& e1) {
-  const uint32_t wx = w ^ 0x88888888u;
+  const uint32_t w7 = w & 0x77777777u;
   const uint32_t w4 = w * 16u;
   const uint32_t m0 = prmt(w4, w, 0xD9C8u);  // 0xFF where the code of K position i (0..3) is >= 8
   const uint32_t m1 = prmt(w4, w, 0xFBEAu);  // the same for K positions 4..7
-  const uint32_t wh = __umulhi(w, 0x10000u), wxh = __umulhi(wx, 0x10000u);
-  e0 = pick(prmt(et.x, et.y, w), prmt(et.z, et.w, wx), m0);
-  e1 = pick(prmt(et.x, et.y, wh), prmt(et.z, et.w, wxh), m1);
+  const uint32_t w7h = __umulhi(w7, 0x10000u);
+  e0 = pick(prmt(et.x, et.y, w7), prmt(et.z, et.w, w7), m0);
+  e1 = pick(prmt(et.x, et.y, w7h), prmt(et.z, et.w, w7h), m1);
 }
 
 // dot products of 16-bit activation pairs with byte lanes (dp2a) and of 8-bit activation quads
@@ -426,11 +426,12 @@ __global__ void __launch_bounds__(kD4Threads, 1)
   }
   __syncthreads();
 
-  // The producer's loads of one stage (and, at a tile's first stage, its e' tables).
-  int seg_p = -1, i_p = 0;
+  // The producer's loads of one stage (and, at a tile's first stage, its e' tables); stages are issued
+  // in order, so the tile t_p and chunk c_p of stage i_p advance by counting (no division per stage).
+  int seg_p = -1, i_p = 0, t_p = u0 / p.cps, c_p = u0 % p.cps;
   bool ok_p = true;
   auto issue = [&](int i, bool may_wait) -> bool {
-    const int u = u0 + i, t = u / p.cps, c = u % p.cps;
+    const int t = t_p, c = c_p;
     if (i == 0 || c == 0) {
       if constexpr (F32) {
         const int tb = (seg_p + 1) & 1;
@@ -453,6 +454,10 @@ __global__ void __launch_bounds__(kD4Threads, 1)
     mbar_arrive_expect_tx(&full[s], Cfg::kStage);
     tma_load_2d(st, &tmC, &full[s], 0, (t * p.cps + c) * 128);
     if constexpr (LPBQ) tma_load_2d(st + kD4Codes, &tmF, &full[s], 0, t * p.fac_rows + c * kD4Steps);
+    if (++c_p == p.cps) {
+      c_p = 0;
+      ++t_p;
+    }
     return true;
   };
   if (warp == 0 && lane == 0) {  // the activation and the first stages start streaming together
@@ -508,8 +513,9 @@ __global__ void __launch_bounds__(kD4Threads, 1)
     const int ch = grp * 32 + lane;
     int64_t tq[MR], te[MR];
     int seg = -1;
+    const int t0 = u0 / p.cps, c0 = u0 % p.cps;  // tile and chunk of this CTA's first stage
+    int t = t0, c = c0;                           // of stage i, advanced by counting
     for (int i = 0; i < nst; ++i) {
-      const int u = u0 + i, t = u / p.cps, c = u % p.cps;
       const bool first = i == 0 || c == 0, last = i == nst - 1 || c == p.cps - 1;
       if (first) {
         ++seg;
@@ -606,12 +612,12 @@ __global__ void __launch_bounds__(kD4Threads, 1)
           red[((kj * 128 + ch) * MR + r) * 2 + 1] = te[r];
         }
         ok = compute_bar_and(ok);
-        const int ca = seg == 0 ? u0 % p.cps : 0;  // first chunk of this segment
+        const int ca = seg == 0 ? c0 : 0;  // first chunk of this segment
         const bool whole = ca == 0 && c == p.cps - 1;
         const int n = t * 128 + ch;
         if (ok && n < p.N) {
           const D4Chan cc = d4_chan<MODE>(p.rec + n);
-          const int slot = (u0 / p.cps == t) ? 0 : 1;
+          const int slot = t0 == t ? 0 : 1;
           for (int r = kj; r < MR && r < p.M; r += kD4KGroups) {
             int64_t Tq = 0, Te = 0;
 #pragma unroll
@@ -627,6 +633,10 @@ __global__ void __launch_bounds__(kD4Threads, 1)
           }
         }
         ok = compute_bar_and(ok);  // the reduction area is free again
+      }
+      if (++c == p.cps) {
+        c = 0;
+        ++t;
       }
     }
   }
