@@ -565,12 +565,13 @@ def cpu_gdn_baseline(A: torch.Tensor, budget_s: float = 10.0) -> dict:
 # ----------------------------------------------------------------------------------------------
 # GEMM rows
 # ----------------------------------------------------------------------------------------------
-def executed_multiplier(op) -> int:
+def executed_multiplier(op, m: int) -> int:
     """Tensor-pipe work per logical op: activation byte planes x weight planes ([q | e'] in the
-    float32-dequant mode, [hi | lo] for int16 weights; one plane in the exact mode).  With the
-    lo-plane residual bound (plan flag 1) the lo activation plane multiplies the q rows only: 3."""
+    float32-dequant mode, [hi | lo] for int16 weights; one plane in the exact mode).  Where the launch
+    uses the lo-plane residual bound (QuantMatMul.lo_residual_launch) the lo activation plane
+    multiplies the q rows only: 3."""
     planes_w = 2 if int(op.plan.mode) in (0, 2) else 1
-    if int(op.plan.mode) == 0 and int(op.plan.a_planes) == 2 and int(op.plan.flags) & 1:
+    if int(op.plan.mode) == 0 and int(op.plan.a_planes) == 2 and op.lo_residual_launch(m):
         return 3
     return int(op.plan.a_planes) * planes_w
 
@@ -609,7 +610,7 @@ def gemm_row(d: dict, args, world: int, rank: int, stream, flush, *, steps: int,
     if m > 128:
         i8, i8_src = int8_peak(pk, probe)
         achieved = 2.0 * m * n_r * k / t_local / 1e12
-        mult = executed_multiplier(op)
+        mult = executed_multiplier(op, m)
         row["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": i8, "unit": "TFLOP/s",
                            "frac": achieved / i8, "op_kind": "int8 MAC x2, logical (2*M*N*K)",
                            "executed_tflops": achieved * mult, "frac_executed": achieved * mult / i8,
@@ -705,7 +706,7 @@ def run_gemm(args, world, rank, local, stream) -> dict:
     e2e_ok = torch.equal(out_h, out.cpu())
     rf = row["roofline"]
     rf["traffic"] = NCU_TRAFFIC_BYTES.get(("qgemm", m, k, d["n"]))
-    rf["kernel"] = ("split_u16_planes + qgemm_kernel<2,F32" + (",LO3" if int(op.plan.flags) & 1 else "") +
+    rf["kernel"] = ("split_u16_planes + qgemm_kernel<2,F32" + (",LO3" if op.lo_residual_launch(m) else "") +
                   "> (one qhtp_matmul_run)")
     res = {
         "metric": "w4a16_lpbq_gemm_tops", "value": ops_total / t_step / 1e12, "unit": "TFLOP/s", "n_gpus": world,

@@ -116,7 +116,7 @@ typedef struct QhtpMatmulPlan {
   double act_scale, out_scale;
   uint64_t act_mant;      /* act_scale = act_mant * 2^act_exp2, 53-bit mantissa */
   int32_t act_exp2;
-  uint32_t flags;         /* kernel options (QHTP_PLAN_FLAG_*); qhtp_matmul_prepare sets the first two */
+  uint32_t flags;         /* kernel options (QHTP_PLAN_FLAG_*), set by qhtp_matmul_prepare but the FORCE_* ones */
   uint64_t out_mant;
   int32_t out_exp2;
   uint64_t plane_bytes;   /* prepared weight planes */
@@ -125,15 +125,22 @@ typedef struct QhtpMatmulPlan {
   void *prepared;         /* device buffer bound by qhtp_matmul_prepare */
 } QhtpMatmulPlan;
 
-/* QhtpMatmulPlan.flags.  LO_RESIDUAL_BY_BOUND: the u16 row-tiled GEMM leaves the lo-plane x e' product
- * out of its MMAs (bounded per channel, exact fix-up near rounding boundaries).  INT4_STREAM: the
- * prepared buffer holds the 4-bit code image (int4 families, per-channel or LPBQ with factors in
- * [1, 16], K % 256 == 0) and runs of M <= 2 rows over a long enough weight stream (at least six
- * 256-deep stages per SM) read it instead of the byte planes.  FORCE_INT4_STREAM: set by the caller
- * before or after prepare; M <= 2 then takes the code stream at any shape (tests, benchmarks). */
+/* QhtpMatmulPlan.flags.  LO_RESIDUAL_BY_BOUND: the lo-plane x e' product of the u16 row-tiled GEMM
+ * is bounded per channel, so the GEMM may leave it out of its MMAs (exact fix-up of the elements near
+ * a rounding boundary).  LO_RESIDUAL_PAYS: the expected fix-ups are few enough (at most ~6 per
+ * 128 x 128 tile on average over the channels) that leaving it out is faster; the GEMM then does so
+ * for launches of at least three waves of tiles (with fewer, the last tile's fix-ups are not hidden
+ * behind a next tile).  INT4_STREAM: the prepared buffer holds the 4-bit code image (int4 families,
+ * per-channel or LPBQ with factors in [1, 16], K % 256 == 0) and runs of M <= 2 rows over a long
+ * enough weight stream (at least six 256-deep stages per SM) read it instead of the byte planes.
+ * FORCE_INT4_STREAM / FORCE_LO_RESIDUAL: set by the caller before or after prepare; M <= 2 then takes
+ * the code stream at any shape, and every row-tiled launch with a valid bound leaves the lo-plane x
+ * e' product out (tests, benchmarks).  Every variant gives the same output bytes. */
 #define QHTP_PLAN_FLAG_LO_RESIDUAL_BY_BOUND 1u
 #define QHTP_PLAN_FLAG_INT4_STREAM 2u
 #define QHTP_PLAN_FLAG_FORCE_INT4_STREAM 4u
+#define QHTP_PLAN_FLAG_LO_RESIDUAL_PAYS 8u
+#define QHTP_PLAN_FLAG_FORCE_LO_RESIDUAL 16u
 
 /* Validate shapes / family / schema and fill *plan (host only, no device access).
  * Requirements: K % 32 == 0, 32 <= K <= 32768, N % 32 == 0, N >= 32; LPBQ only for int4 families. */

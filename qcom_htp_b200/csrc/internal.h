@@ -20,10 +20,18 @@ enum GemmMode : uint32_t {
 };
 
 // QhtpMatmulPlan.flags (set by qhtp_matmul_prepare)
-constexpr uint32_t kPlanLoResidualByBound = 1u;  // the lo-plane x e' product is left out of the MMAs and
-                                                 // bounded per channel (ChannelRecord::lo_win); elements
-                                                 // within that bound of a rounding boundary get it exactly
+constexpr uint32_t kPlanLoResidualByBound = 1u;  // the lo-plane x e' product is bounded per channel
+                                                 // (ChannelRecord::lo_win), so the GEMM may leave it out of
+                                                 // the MMAs; elements within that bound of a rounding
+                                                 // boundary then get it exactly
 constexpr int32_t kLoWinMax = 1 << 20;           // widest per-channel window that enables it (~1e-3 units)
+constexpr uint32_t kPlanLoResidualPays = 8u;     // mean window <= kLoWinMeanMax: the bound is worth using
+constexpr uint32_t kPlanForceLoResidual = 16u;   // set by the caller: use the bound on every launch
+// A value is sent to the exact fix-up with probability ~2 (lo_win + 2) / 2^30, so a 128 x 128 tile
+// expects 2^15 (mean lo_win + 2) / 2^30 fix-ups; 3 * 2^16 is ~6 per tile.  Measured on B200 at
+// K = 4096: ~3 per tile (W4A16) gains 8 %, ~8.5 (W8A16) loses 5 %.
+constexpr uint64_t kLoWinMeanMax = 3u << 16;
+constexpr int kLoResidualMinWaves = 3;           // row-tiled launches of fewer waves keep the full product
 constexpr uint32_t kPlanInt4Stream = 2u;         // the int4 code image was built (qdec4.cu): decode rows
                                                  // stream 4-bit codes instead of the byte planes
 constexpr uint32_t kPlanForceInt4Stream = 4u;    // set by the caller: M <= 2 takes the code stream at any shape

@@ -108,6 +108,10 @@ struct GemmParams {
   int* err;
 };
 
+#ifndef QHTP_LO_DOT_BATCH
+#define QHTP_LO_DOT_BATCH 8  // chunks per lane in flight in the exact lo x e' fix-up
+#endif
+
 constexpr int kEpiWarps = 8;
 constexpr int kEpiWarp0 = 4;  // first epilogue warp (warpgroups 1 and 2)
 constexpr int kGemmThreads = 32 * (kEpiWarp0 + kEpiWarps);
@@ -155,21 +159,39 @@ __device__ __forceinline__ bool epi_bar_and(bool v) {
 }
 
 // sum_k x_lo[mm, k] * e'[nn, k] over the real K, by the whole warp (lane l takes the 16-byte chunks
-// l, l + 32, ...: u8 activation bytes times s8 residuals, 4 per dp4a), returned to every lane.
+// l, l + 32, ...: u8 activation bytes times s8 residuals, 4 per dp4a), returned to every lane.  A
+// lane's chunks are loaded kLoDotBatch at a time, all in flight together: the fix-up sits in the
+// epilogue, and in a launch of one or two tiles per CTA its latency is the kernel's.
+constexpr int kLoDotBatch = QHTP_LO_DOT_BATCH;
+__device__ __forceinline__ void lo_dot16(int32_t& acc, const uint4& xv, const uint4& ev) {
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.x), "r"(ev.x));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.y), "r"(ev.y));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.z), "r"(ev.z));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.w), "r"(ev.w));
+}
 __device__ __forceinline__ int32_t lo_residual_dot(const GemmParams& p, int mm, int nn, int lane) {
+  constexpr int B = kLoDotBatch;
   const uint8_t* xr = p.a_lo + static_cast<size_t>(mm) * p.K;
   const int nt = nn / kTileN, rr = nn % kTileN;
   const int8_t* wr = p.wplanes + (static_cast<size_t>(nt) * p.kblocks * 256 + 128 + rr) * kTileK;
+  auto e_at = [&](int ch) {
+    return *reinterpret_cast<const uint4*>(wr + static_cast<size_t>(ch >> 3) * 256 * kTileK +
+                                           ((((ch & 7) ^ rr) & 7) << 4));
+  };
+  const int nch = p.K / 16;
   int32_t acc = 0;
-  for (int ch = lane; ch < p.K / 16; ch += 32) {
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + ch * 16);
-    const uint4 ev = *reinterpret_cast<const uint4*>(wr + static_cast<size_t>(ch >> 3) * 256 * kTileK +
-                                                     ((((ch & 7) ^ rr) & 7) << 4));
-    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.x), "r"(ev.x));
-    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.y), "r"(ev.y));
-    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.z), "r"(ev.z));
-    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(xv.w), "r"(ev.w));
+  int ch = lane;
+  for (; ch + 32 * (B - 1) < nch; ch += 32 * B) {
+    uint4 xv[B], ev[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      xv[u] = *reinterpret_cast<const uint4*>(xr + (ch + 32 * u) * 16);
+      ev[u] = e_at(ch + 32 * u);
+    }
+#pragma unroll
+    for (int u = 0; u < B; ++u) lo_dot16(acc, xv[u], ev[u]);
   }
+  for (; ch < nch; ch += 32) lo_dot16(acc, *reinterpret_cast<const uint4*>(xr + ch * 16), e_at(ch));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   return acc;
@@ -629,6 +651,18 @@ cudaError_t launch_split_u16(const uint16_t* act, uint8_t* planes, size_t total,
   return cudaGetLastError();
 }
 
+// The lo-plane residual bound on a row-tiled launch of `tiles` tiles: where it is valid and either
+// forced by the caller, or worth it (few expected fix-ups) on a launch of at least
+// kLoResidualMinWaves waves -- with fewer, the last tile's fix-ups are not hidden behind a next
+// tile's MMAs (measured: M = 128, N = 14336 in one wave 48.2 us with it, 42.0 us without).
+static bool lo_residual_launch(const QhtpMatmulPlan* pl, int tiles, uint32_t max_ctas) {
+  if (!(pl->flags & kPlanLoResidualByBound)) return false;
+  if (pl->flags & kPlanForceLoResidual) return true;
+  int slots = sm_count();
+  if (max_ctas != 0 && static_cast<int>(max_ctas) < slots) slots = static_cast<int>(max_ctas);
+  return (pl->flags & kPlanLoResidualPays) && tiles >= kLoResidualMinWaves * slots;
+}
+
 cudaError_t launch_gemm(const GemmLaunch& g) {
   const QhtpMatmulPlan* pl = g.plan;
   const uint32_t K = pl->k;
@@ -674,7 +708,8 @@ cudaError_t launch_gemm(const GemmLaunch& g) {
   switch (pl->mode * 2 + (pl->a_planes - 1)) {
     case kModeF32 * 2 + 0: return launch_variant<1, kModeF32>(g, ta, tb, prm);
     case kModeF32 * 2 + 1:
-      if (pl->flags & kPlanLoResidualByBound) return launch_variant<2, kModeF32, true>(g, ta, tb, prm);
+      if (lo_residual_launch(pl, prm.m_tiles * prm.n_tiles, g.max_ctas))
+        return launch_variant<2, kModeF32, true>(g, ta, tb, prm);
       return launch_variant<2, kModeF32>(g, ta, tb, prm);
     case kModeExact * 2 + 0: return launch_variant<1, kModeExact>(g, ta, tb, prm);
     case kModeExact * 2 + 1: return launch_variant<2, kModeExact>(g, ta, tb, prm);
@@ -802,6 +837,7 @@ __global__ void prepare_records_kernel(uint32_t mode, uint32_t N, const float* _
       const double x = __dmul_rn(__dmul_rn(static_cast<double>(255 * sa), c), 1073741824.0);
       r.lo_win = x >= 1073741824.0 ? (1 << 30) : static_cast<int32_t>(ceil(x)) + 1;
       atomicMax(bad_scale + 1, r.lo_win);
+      atomicAdd(reinterpret_cast<unsigned long long*>(bad_scale + 4), static_cast<unsigned long long>(r.lo_win));
     }
   } else {
     r.beff = b - static_cast<int64_t>(act_zp) * sq;

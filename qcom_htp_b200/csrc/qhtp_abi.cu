@@ -249,15 +249,20 @@ QhtpStatus qhtp_matmul_prepare(QhtpMatmulPlan* plan, const QhtpMatmulWeights* w,
   cudaError_t e = launch_prepare(plan, w, prepared, dflag, s);
   if (e == cudaSuccess) e = launch_prepare_int4(plan, w, prepared, dflag, s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
-  // [0] bad-scale flag, [1] widest per-channel lo-plane residual window, [2] LPBQ factor outside [1, 16]
-  int h[3] = {0, 0, 0};
+  // [0] bad-scale flag, [1] widest per-channel lo-plane residual window, [2] LPBQ factor outside [1, 16],
+  // [4..5] sum of the channels' windows (uint64)
+  int h[6] = {0, 0, 0, 0, 0, 0};
   e = cudaMemcpyAsync(h, dflag, sizeof(h), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return QHTP_STATUS_RUNTIME_ERROR;
   if (h[0] != 0) return QHTP_STATUS_INVALID_ARGUMENT;  // a scale was zero, negative, subnormal or not finite
-  plan->flags &= kPlanForceInt4Stream;  // the caller's dispatch override survives a re-prepare
-  if (plan->mode == kModeF32 && plan->a_planes == 2 && h[1] > 0 && h[1] <= kLoWinMax)
+  plan->flags &= kPlanForceInt4Stream | kPlanForceLoResidual;  // the caller's overrides survive a re-prepare
+  if (plan->mode == kModeF32 && plan->a_planes == 2 && h[1] > 0 && h[1] <= kLoWinMax) {
     plan->flags |= kPlanLoResidualByBound;
+    const uint64_t win_sum = static_cast<uint64_t>(static_cast<uint32_t>(h[4])) |
+                             (static_cast<uint64_t>(static_cast<uint32_t>(h[5])) << 32);
+    if (win_sum <= kLoWinMeanMax * plan->n) plan->flags |= kPlanLoResidualPays;
+  }
   if (int4_stream_layout(plan) && h[2] == 0) plan->flags |= kPlanInt4Stream;
   plan->prepared = prepared;
   return QHTP_STATUS_OK;

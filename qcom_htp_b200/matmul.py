@@ -197,6 +197,22 @@ class QuantMatMul:
         if st != L.OK:
             raise L.QhtpError(f"qhtp_matmul_check (device code {code.value})", st)
 
+    def lo_residual_launch(self, m: int, max_ctas: int = 0) -> bool:
+        """Whether a row-tiled launch over M rows leaves the lo-plane x e' product out of its MMAs (the
+        library's rule, qgemm.cu lo_residual_launch): the bound is valid (plan flag 1) and either the
+        caller forces it (flag 16) or prepare found it worth it (flag 8) and the launch has at least
+        three waves of 128 x 128 tiles on the SMs it may use.  Descriptive only: outputs are the same."""
+        f = int(self.plan.flags)
+        if not f & 1:
+            return False
+        if f & 16:
+            return True
+        slots = torch.cuda.get_device_properties(self.device).multi_processor_count
+        if 0 < max_ctas < slots:
+            slots = max_ctas
+        tiles = ((m + 127) // 128) * int(self.plan.n_tiles)
+        return bool(f & 8) and tiles >= 3 * slots
+
     def scratch_bytes(self, m: int, chain: int = 1) -> int:
         """Device scratch bytes run_prepared needs for M rows (qhtp_prepared_run_scratch_bytes)."""
         return int(L.lib.qhtp_prepared_run_scratch_bytes(C.byref(self.plan), m, chain))
