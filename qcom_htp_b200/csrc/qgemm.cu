@@ -118,6 +118,14 @@ constexpr int kGemmThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr int kRegsLaunch = 168, kRegsCtrl = 40, kRegsEpi = 232;
 static_assert(kGemmThreads * kRegsLaunch == 128 * kRegsCtrl + 32 * kEpiWarps * kRegsEpi, "register split");
 
+// 16-byte global -> shared copy that bypasses the registers (completed by cp_async_wait).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <int N>
 __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
@@ -140,8 +148,8 @@ struct GemmCfg {
   static constexpr int kStage = PA * kStageA + kStageB;
   static constexpr int kStagesRaw = (200 * 1024) / kStage;
   static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
-  static constexpr int kRecBytes = kTileN * 32;  // the tile's channel records, staged for the epilogue
-  static constexpr int kSmem = kStages * kStage + kRecBytes + 1024 + 256;
+  static constexpr int kRecBytes = kTileN * 32;  // a tile's channel records, staged for the epilogue
+  static constexpr int kSmem = kStages * kStage + 2 * kRecBytes + 1024 + 256;  // two record buffers
 };
 
 // Named barrier 1 over the epilogue warps, and the same barrier ANDing a predicate (every thread
@@ -212,8 +220,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  ChannelRecord* rec_s = reinterpret_cast<ChannelRecord*>(smem + S * Cfg::kStage);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage + Cfg::kRecBytes);
+  ChannelRecord* rec_s = reinterpret_cast<ChannelRecord*>(smem + S * Cfg::kStage);  // [2][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage + 2 * Cfg::kRecBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 1;      // [2]: TMEM half A / half B handed back by the epilogue
@@ -379,20 +387,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - kEpiWarp0) >> 2;  // which 64 of the 128 channels
     const int row = quad * 32 + lane;
     const bool u16 = p.qmax > 255;
+    // A tile's 128 channel records (4 KB) are copied into shared memory (cp.async, 16 bytes per
+    // thread) one tile ahead, into the other of two buffers: the drain and the requant read their
+    // constants there, and the copy's latency hides behind the previous tile's requant.
+    const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..255, 16 bytes each
+    auto stage_records = [&](int t, uint32_t buf) {
+      if (t < total_tiles)
+        cp_async16(smem_u32(rec_s + buf * kTileN) + 16 * et,
+                   reinterpret_cast<const uint4*>(p.rec + (t / p.m_tiles) * kTileN) + et);
+      cp_async_commit();  // an empty group past the last tile keeps the group count per tile
+    };
+    stage_records(blockIdx.x, 0);
     uint32_t tc = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
       const int m = (tile % p.m_tiles) * kTileM + row;
       const int n0 = (tile / p.m_tiles) * kTileN + half * 64;
-      // The tile's 128 channel records (4 KB) -> shared memory while the accumulators are still being
-      // formed: the drain and the requant read their constants there, not from L2.
-      epi_bar();  // every epilogue warp is done with the previous tile's records
-      {
-        const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..255, 16 bytes each
-        reinterpret_cast<uint4*>(rec_s)[et] =
-            __ldg(reinterpret_cast<const uint4*>(p.rec + (tile / p.m_tiles) * kTileN) + et);
-      }
-      if (!epi_bar_and(mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum))) break;  // also publishes rec_s
-      const ChannelRecord* rec = rec_s + half * 64;
+      epi_bar();  // every epilogue warp is done with the previous tile's records (the other buffer)
+      stage_records(tile + gridDim.x, (tc + 1) & 1);
+      cp_async_wait<1>();  // this tile's records (all but the newest group) have landed
+      if (!epi_bar_and(mbar_wait(tfull, tc & 1, p.err, kErrTimeoutAccum))) break;  // also publishes them
+      const ChannelRecord* rec = rec_s + (tc & 1) * kTileN + half * 64;
       tc_fence_after();
       const uint32_t tl = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
       // ---- drain: TMEM -> int64 accumulators in registers (64 channels of this thread's row).  The
@@ -580,6 +594,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = 0; j < 48; ++j) T[j] = T[j + 16];
       }
     }
+    cp_async_wait<0>();  // no record copy is still in flight when the CTA's shared memory goes away
   }
   tc_fence_before();
   __syncthreads();
