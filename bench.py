@@ -57,7 +57,7 @@ L2_FLUSH_BYTES = 256 << 20
 # of this script's own workload (the command is in the profiles/ summary of each kernel); the GDN
 # figures are 1024-chunk captures scaled by the chunk count (traffic grows with the chunks)
 NCU_TRAFFIC_BYTES = {
-    ("qgemm", 4096, 4096, 14336): 152_510_720 + 99_488_512,           # full-size capture (LO3 variant)
+    ("qgemm", 4096, 4096, 14336): 153_400_832 + 100_256_768,          # full-size capture (LO3 variant)
     ("gdn_per_chunk",): (100_822_016 + 208_797_696) / 1024,            # 1024-chunk capture
     ("gdn_fused_per_chunk",): (69_339_904 + 208_701_952) / 1024,       # 1024-chunk capture
     ("qdecode", 16, 4096, 14336): 118_091_264 + 4_662_784,             # full-size capture
