@@ -578,14 +578,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 v.y = cd[2] | (cd[3] << 16);
                 v.z = cd[4] | (cd[5] << 16);
                 v.w = cd[6] | (cd[7] << 16);
-                *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N + n +
-                                          8 * h) = v;
+                // streaming (evict-first) store: the output does not displace the operand tiles in L2
+                __stcs(reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<size_t>(m) * p.N +
+                                                n + 8 * h), v);
               } else {
                 uint2 v;
                 v.x = cd[0] | (cd[1] << 8) | (cd[2] << 16) | (cd[3] << 24);
                 v.y = cd[4] | (cd[5] << 8) | (cd[6] << 16) | (cd[7] << 24);
-                *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N + n +
-                                          8 * h) = v;
+                __stcs(reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + static_cast<size_t>(m) * p.N +
+                                                n + 8 * h), v);
               }
             }
           }
